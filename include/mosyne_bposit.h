@@ -1,0 +1,237 @@
+/* mosyne_bposit.h -- C ABI of libmosyne_bposit.so (B200 / sm_100a build).
+ *
+ * The first block is the reference's shipped ABI, symbol for symbol
+ * (packages/mosyne_bposit/src/mosyne_bposit/_cuda/libmosyne_bposit.cu):
+ * same names, argument meaning, layouts (column-major x[M,K], w[K,N],
+ * y[M,N]), return codes, and stream semantics (legacy default stream, no
+ * synchronisation).  Everything after it is an addition with no counterpart
+ * in the reference's C ABI; each cites the reference code whose behaviour it
+ * exposes.
+ *
+ * Return codes: 0 ok; -1 launch error; -2 GEMM launch failure; -10 library
+ * not initialised; -11 scratch allocation failed; -20 invalid argument;
+ * -30 a device-side wait gave up (see mosyne_bposit_last_error).
+ *
+ * All pointers are device pointers unless the name says _host.  bf16 and
+ * fp16 buffers are passed as 16-bit words (binary compatible with
+ * __nv_bfloat16 / __half).
+ */
+#ifndef MOSYNE_BPOSIT_H
+#define MOSYNE_BPOSIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t mosyne_bf16_t;
+typedef uint16_t mosyne_fp16_t;
+typedef void* mosyne_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* 256-bit two's-complement fixed point, 96 fraction bits, little-endian
+ * words (kernels/bposit16_encode.cuh:30). */
+typedef struct mosyne_quire256 {
+  uint64_t w[4];
+} mosyne_quire256;
+
+/* ------------------------------------------------------------------------
+ * Reference ABI (libmosyne_bposit.cu)
+ * ------------------------------------------------------------------------ */
+
+/* libmosyne_bposit.cu:95 -- idempotent; 0 on success. */
+int mosyne_bposit_init(void);
+
+/* libmosyne_bposit.cu:145 -- frees all cached state; safe to repeat. */
+void mosyne_bposit_shutdown(void);
+
+/* libmosyne_bposit.cu:183 -- w column-major [K,N] fp32 -> int8 [K,N] and
+ * w_scale[N] = 127/max|w[:,n]| (1.0 for an all-zero column).  Does not
+ * require init. */
+int mosyne_bposit_quantize_weight_per_channel(const float* w_fp32, int K, int N,
+                                              int8_t* w_i8_out, float* w_scale_out);
+
+/* libmosyne_bposit.cu:322 -- y[M,N] = (x_q @ w_i8) / (x_scale[m] * w_scale[n]),
+ * per-token activation quantisation inside; all column-major. */
+int mosyne_bposit_linear_w8a8(const float* d_x_fp32, int M, int K, const int8_t* d_w_i8,
+                              const float* d_w_scale, int N, float* d_y_fp32);
+
+/* libmosyne_bposit.cu:354 -- bf16 x, fp32 y. */
+int mosyne_bposit_linear_w8a8_bf16(const mosyne_bf16_t* d_x_bf16, int M, int K,
+                                   const int8_t* d_w_i8, const float* d_w_scale, int N,
+                                   float* d_y_fp32);
+
+/* libmosyne_bposit.cu:383 -- bf16 x, bf16 y. */
+int mosyne_bposit_linear_w8a8_bf16_io(const mosyne_bf16_t* d_x_bf16, int M, int K,
+                                      const int8_t* d_w_i8, const float* d_w_scale, int N,
+                                      mosyne_bf16_t* d_y_bf16);
+
+/* libmosyne_bposit.cu:412 -- fp16 x, fp32 y. */
+int mosyne_bposit_linear_w8a8_fp16(const mosyne_fp16_t* d_x_fp16, int M, int K,
+                                   const int8_t* d_w_i8, const float* d_w_scale, int N,
+                                   float* d_y_fp32);
+
+/* libmosyne_bposit.cu:440 -- fp16 x, fp16 y. */
+int mosyne_bposit_linear_w8a8_fp16_io(const mosyne_fp16_t* d_x_fp16, int M, int K,
+                                      const int8_t* d_w_i8, const float* d_w_scale, int N,
+                                      mosyne_fp16_t* d_y_fp16);
+
+/* libmosyne_bposit.cu:466 -- host round trip: auto-init, upload x and the fp32
+ * weight, quantise the weight per call, run, copy y back (synchronous). */
+int mosyne_bposit_linear_w8a8_host(const float* host_x, int M, int K, const float* host_w,
+                                   int N, float* host_y);
+
+/* ------------------------------------------------------------------------
+ * Additions (no counterpart in the reference's C ABI)
+ * ------------------------------------------------------------------------ */
+
+/* dtype codes */
+#define MOSYNE_DT_F32 0
+#define MOSYNE_DT_BF16 1
+#define MOSYNE_DT_F16 2
+#define MOSYNE_DT_F64 3
+
+/* flags */
+#define MOSYNE_RTNE_BP32 0x1     /* bposit32 outputs round to nearest even (default: truncate) */
+#define MOSYNE_RTNE_BP16 0x2     /* bposit16 outputs round to nearest even (default: truncate) */
+#define MOSYNE_XS_SCALAR 0x4     /* x_scale is one value (per-tensor) */
+#define MOSYNE_WS_SCALAR 0x8     /* w_scale is one value (per-tensor) */
+#define MOSYNE_OUT_ROW_MAJOR 0x10 /* outputs row-major [M,N] instead of column-major */
+#define MOSYNE_X_ROW_MAJOR 0x20  /* linear: x is row-major [M,K] instead of column-major */
+#define MOSYNE_X_PER_TENSOR 0x40 /* linear: one activation scale for the whole x */
+
+/* Version string of this build. */
+const char* mosyne_bposit_version(void);
+
+/* Synchronises the current device and reports (then clears) the device error
+ * word: 0 if every device-side wait completed, -30 if one gave up, or a CUDA
+ * error as -1. */
+int mosyne_bposit_last_error(void);
+
+/* Diagnostic: launches one bounded device-side wait that nothing satisfies;
+ * it gives up after limit_ns (capped at 2 s) and sets the device error word,
+ * so the next mosyne_bposit_last_error() returns -30.  Exercises the
+ * give-up path of every pipeline wait without hanging the GPU. */
+int mosyne_bposit_debug_wait_timeout(unsigned long long limit_ns, mosyne_stream_t stream);
+
+/* Fused INT8 GEMM, kernels/test_mera_isometry_imma.cu:277-352 (cuBLASLt GEMM
+ * + int32 -> bposit32 epilogue) and libmosyne_bposit.cu:252-319 (IMMA +
+ * dequant) in one tcgen05 kernel:
+ *   acc[m,n] = sum_k A[m,k] * B[n,k]          (exact INT32)
+ *   out_bp32 = bposit32(acc)   == quire256_to_bposit32(acc << 96)
+ *   out_bp16 = bposit16(acc)
+ *   out_f32  = (float)acc / (x_scale[m] * w_scale[n])
+ *   out_i32  = acc
+ * A is [M,K] with K contiguous; B is [N,K] with K contiguous (= column-major
+ * [K,N]).  Any output pointer may be NULL (skipped).  Outputs are
+ * column-major [M,N] unless MOSYNE_OUT_ROW_MAJOR.  y_dtype selects the
+ * dequant output type (MOSYNE_DT_F32/BF16/F16) written to out_y. */
+int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
+                          const float* x_scale, const float* w_scale, uint32_t* out_bp32,
+                          uint16_t* out_bp16, void* out_y, int y_dtype, int32_t* out_i32,
+                          int flags, mosyne_stream_t stream);
+
+/* Host-buffer round trip of mosyne_bposit_gemm_i8 (A, B and outputs in host
+ * memory; synchronous), the end-to-end form of the GEMM. */
+int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, int K,
+                               uint32_t* out_bp32, int32_t* out_i32, int flags);
+
+/* W8A8 linear with every option: x dtype (MOSYNE_DT_*), x layout
+ * (MOSYNE_X_ROW_MAJOR), per-token or per-tensor activation scale
+ * (MOSYNE_X_PER_TENSOR), dequant output y (y_dtype; may be NULL), raw
+ * dot-product bposit32/bposit16 outputs (may be NULL), stream.  The
+ * reference's five device entry points are this call with fixed options. */
+int mosyne_bposit_linear_w8a8_ex(const void* x, int x_dtype, int M, int K,
+                                 const int8_t* w_i8, const float* w_scale, int N,
+                                 void* y, int y_dtype, uint32_t* y_bp32, uint16_t* y_bp16,
+                                 int flags, mosyne_stream_t stream);
+
+/* libmosyne_bposit.cu:206-244: per-token quantisation of x [M,K] (column-major,
+ * or row-major with MOSYNE_X_ROW_MAJOR) to x_i8 [M,K] with K contiguous and
+ * x_scale[M]. */
+int mosyne_bposit_quantize_per_token(const void* x, int x_dtype, int M, int K, int8_t* x_i8,
+                                     float* x_scale, int flags, mosyne_stream_t stream);
+
+/* Per-tensor quantisation (scale = 127/max|t|, the per-token convention) of a
+ * [rows, cols] tensor.  With MOSYNE_X_ROW_MAJOR the input is row-major,
+ * otherwise column-major; the output is always row-major [rows, cols]
+ * (K contiguous when rows = M, cols = K). */
+int mosyne_bposit_quantize_per_tensor(const void* t, int dtype, int rows, int cols,
+                                      int8_t* q, float* scale, int flags,
+                                      mosyne_stream_t stream);
+
+/* libmosyne_bposit.cu:162-193 on a stream, for fp32/bf16/fp16 weights. */
+int mosyne_bposit_quantize_weight_per_channel_ex(const void* w, int dtype, int K, int N,
+                                                 int8_t* w_i8_out, float* w_scale_out,
+                                                 mosyne_stream_t stream);
+
+/* Exact (order independent) sum of n bposit16 codes in quire256
+ * (kernels/test_determinism_headline.cu:65-97, shannon_entropy_bposit16.cu:
+ * 45-119): writes the quire and its bposit16 / bposit32 encodings (any output
+ * may be NULL).  flags: MOSYNE_RTNE_BP16 / MOSYNE_RTNE_BP32. */
+int mosyne_bposit_quire_sum_bp16(const uint16_t* x, size_t n, mosyne_quire256* q_out,
+                                 uint16_t* bp16_out, uint32_t* bp32_out, int flags,
+                                 mosyne_stream_t stream);
+
+/* kernels/test_determinism_headline.cu:56-60: fp32 atomicAdd control sum
+ * into *acc (not zeroed by the call). */
+int mosyne_bposit_fp32_atomic_sum(const float* x, size_t n, float* acc, mosyne_stream_t stream);
+
+/* kernels/bposit16_encode.cuh:113-418: element-wise quire256 -> bposit. */
+int mosyne_bposit_quire_to_bp16(const mosyne_quire256* q, size_t n, uint16_t* out, int rtne,
+                                mosyne_stream_t stream);
+int mosyne_bposit_quire_to_bp32(const mosyne_quire256* q, size_t n, uint32_t* out, int rtne,
+                                mosyne_stream_t stream);
+
+/* kernels/bposit16_encode.cuh:424-431: element-wise bposit16 -> quire256. */
+int mosyne_bposit_bp16_to_quire(const uint16_t* x, size_t n, mosyne_quire256* out,
+                                mosyne_stream_t stream);
+
+/* kernels/test_int32_to_bposit32.cu:94-126: value = in / 2^scale_shift. */
+int mosyne_bposit_int32_to_bp32(const int32_t* in, size_t n, int scale_shift, uint32_t* out,
+                                int rtne, mosyne_stream_t stream);
+
+/* kernels/bposit16_reference.py:485-503 (exact value of each binary float):
+ * x of dtype MOSYNE_DT_F32 or MOSYNE_DT_F64 -> bposit16 (nbits 16, uint16
+ * out) or bposit32 (nbits 32, uint32 out). */
+int mosyne_bposit_float_to_bposit(const void* x, int dtype, size_t n, void* out, int nbits,
+                                  int rtne, mosyne_stream_t stream);
+
+/* Standalone W8A8 epilogue over an INT32 accumulator acc [M,N] (column-major),
+ * used after an exact cross-GPU INT32 reduction (K-split): same outputs and
+ * flags as mosyne_bposit_gemm_i8. */
+int mosyne_bposit_epilogue_i32(const int32_t* acc, int M, int N, const float* x_scale,
+                               const float* w_scale, uint32_t* out_bp32, uint16_t* out_bp16,
+                               void* out_y, int y_dtype, int flags, mosyne_stream_t stream);
+
+/* bposit16 ALU, element-wise over n codes.
+ * add: kernels/bposit16_encode.cuh:472-483 (exact via quire256);
+ * mul: bposit16_encode.cuh:491-537 (log2 + quire add + exp2 tables);
+ * mul_exact: kernels/bposit16_reference.py:507-516 (exact product, truncated);
+ * neg: bposit16_encode.cuh:437-443 (two's complement) or, with
+ *      ones_complement != 0, 461-467;
+ * recip/sqrt/log2/exp2: the 65,536-entry tables of
+ *      kernels/build_bposit_luts.py:34-259. */
+int mosyne_bposit16_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out,
+                        mosyne_stream_t stream);
+int mosyne_bposit16_mul(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out,
+                        mosyne_stream_t stream);
+int mosyne_bposit16_mul_exact(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out,
+                              mosyne_stream_t stream);
+int mosyne_bposit16_neg(const uint16_t* a, size_t n, uint16_t* out, int ones_complement,
+                        mosyne_stream_t stream);
+int mosyne_bposit16_recip(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
+int mosyne_bposit16_sqrt(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
+int mosyne_bposit16_log2(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
+int mosyne_bposit16_exp2(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
+
+/* Copies one of the device-resident ALU tables (0 log2, 1 exp2, 2 sqrt,
+ * 3 recip; 65,536 u16) to host memory, for verification. */
+int mosyne_bposit16_table_host(int which, uint16_t* host_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOSYNE_BPOSIT_H */

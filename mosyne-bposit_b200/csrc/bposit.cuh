@@ -1,0 +1,301 @@
+// bposit.cuh -- bounded-posit (bposit8/16/32, es=3, useed=256) encoders,
+// decoders and the quire256 exact accumulator, for device and host code.
+//
+// Format (kernels/bposit16_reference.py:22-36, 378-503; 93-146):
+//   value = 256^k * 2^e * (1.f),  scale = 8k + e clamped to [-48, 48];
+//   regime k>=0: (k+1) ones then a 0;  k<0: (-k) zeros then a 1;
+//   3 exponent bits, then the fraction; negative values are the two's
+//   complement of the (n-1)-bit magnitude field; 0x80..0 is NaR.
+// Default rounding truncates the fraction (the reference's default,
+// kernels/bposit16_encode.cuh:179-183); RTNE uses the round bit and sticky
+// bits with a saturating increment (bposit16_encode.cuh:299-311).
+//
+// quire256 (bposit16_encode.cuh:27-30): 256-bit two's complement integer,
+// four little-endian u64 words, 96 fraction bits.
+#pragma once
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define BP_HD __host__ __device__ __forceinline__
+#else
+#define BP_HD inline
+#endif
+
+namespace bp {
+
+constexpr int kQuireFracBits = 96;
+constexpr int kScaleLimit = 48;
+
+BP_HD int clz32(uint32_t x) {
+#if defined(__CUDA_ARCH__)
+  return __clz(x);
+#else
+  return x ? __builtin_clz(x) : 32;
+#endif
+}
+BP_HD int clz64(uint64_t x) {
+#if defined(__CUDA_ARCH__)
+  return __clzll(x);
+#else
+  return x ? __builtin_clzll(x) : 64;
+#endif
+}
+
+// Magnitude field (n-1 bits) of a positive value with floor(log2) = scale,
+// fraction bits frac64 (MSB-aligned: bit 63 is the first bit below the
+// leading one) and `sticky` = any non-zero bit beyond those 64.
+template <int NBITS>
+BP_HD uint32_t encode_field(int scale, uint64_t frac64, bool sticky, bool rtne) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  if (scale > kScaleLimit) return FMASK;   // +maxpos
+  if (scale < -kScaleLimit) return 1u;     // +minpos
+  const int k = scale >> 3;                // floor(scale / 8)
+  const int e = scale & 7;
+  int rlen;
+  uint32_t regime;
+  if (k >= 0) {
+    rlen = k + 2;
+    regime = ((2u << k) - 1u) << (N1 - (k + 1));
+  } else {
+    rlen = 1 - k;
+    regime = 1u << (N1 - rlen);
+  }
+  const int fw = N1 - rlen - 3;            // >= 4 for bposit16, >= 20 for bposit32
+  const uint32_t f = (uint32_t)(frac64 >> (64 - fw));
+  uint32_t field = regime | ((uint32_t)e << fw) | f;
+  if (rtne) {
+    const uint64_t rest = frac64 << fw;    // bits after the kept fraction
+    const bool rbit = (rest >> 63) != 0;
+    const bool st = sticky || ((rest << 1) != 0);
+    if (rbit && (st || (f & 1u)) && field < FMASK) field += 1u;
+  }
+  return field;
+}
+
+template <int NBITS>
+BP_HD uint32_t apply_sign(uint32_t field, bool neg) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  return neg ? ((1u << N1) | ((0u - field) & FMASK)) : field;
+}
+
+// bposit<NBITS> of the exact value I / 2^shift (I any int64, |I| <= 2^63).
+template <int NBITS>
+BP_HD uint32_t from_int64(int64_t I, int shift, bool rtne) {
+  if (I == 0) return 0u;
+  const bool neg = I < 0;
+  const uint64_t a = neg ? (uint64_t)0 - (uint64_t)I : (uint64_t)I;
+  const int lz = clz64(a);
+  const int msb = 63 - lz;
+  const uint64_t frac = (a << lz) << 1;    // drop the leading one
+  return apply_sign<NBITS>(encode_field<NBITS>(msb - shift, frac, false, rtne), neg);
+}
+
+// Fast path for an INT32 accumulator (value = I, no fraction bits):
+// int_to_bposit32(I, 0) of kernels/test_int32_to_bposit32.cu:94-112, equal
+// to quire256_to_bposit32(I << 96).  scale = msb in [0, 31] never saturates.
+template <int NBITS>
+BP_HD uint32_t from_int32(int32_t I, bool rtne) {
+  if (I == 0) return 0u;
+  const bool neg = I < 0;
+  const uint32_t a = neg ? 0u - (uint32_t)I : (uint32_t)I;
+  const int lz = clz32(a);
+  const uint64_t frac = (uint64_t)((a << lz) << 1) << 32;
+  return apply_sign<NBITS>(encode_field<NBITS>(31 - lz, frac, false, rtne), neg);
+}
+
+// ---------------------------------------------------------------------------
+// quire256
+// ---------------------------------------------------------------------------
+struct quire256 {
+  uint64_t w[4];
+};
+
+BP_HD quire256 q_zero() { return quire256{{0, 0, 0, 0}}; }
+
+BP_HD quire256 q_add(const quire256& a, const quire256& b) {
+  quire256 r;
+#if defined(__CUDA_ARCH__)
+  asm("add.cc.u64 %0, %4, %8;\n\t"
+      "addc.cc.u64 %1, %5, %9;\n\t"
+      "addc.cc.u64 %2, %6, %10;\n\t"
+      "addc.u64 %3, %7, %11;\n\t"
+      : "=l"(r.w[0]), "=l"(r.w[1]), "=l"(r.w[2]), "=l"(r.w[3])
+      : "l"(a.w[0]), "l"(a.w[1]), "l"(a.w[2]), "l"(a.w[3]),
+        "l"(b.w[0]), "l"(b.w[1]), "l"(b.w[2]), "l"(b.w[3]));
+#else
+  uint64_t c = 0;
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t s = a.w[i] + b.w[i];
+    const uint64_t c1 = s < a.w[i];
+    r.w[i] = s + c;
+    c = c1 | (r.w[i] < s);
+  }
+#endif
+  return r;
+}
+
+BP_HD quire256 q_sub(const quire256& a, const quire256& b) {
+  quire256 r;
+#if defined(__CUDA_ARCH__)
+  asm("sub.cc.u64 %0, %4, %8;\n\t"
+      "subc.cc.u64 %1, %5, %9;\n\t"
+      "subc.cc.u64 %2, %6, %10;\n\t"
+      "subc.u64 %3, %7, %11;\n\t"
+      : "=l"(r.w[0]), "=l"(r.w[1]), "=l"(r.w[2]), "=l"(r.w[3])
+      : "l"(a.w[0]), "l"(a.w[1]), "l"(a.w[2]), "l"(a.w[3]),
+        "l"(b.w[0]), "l"(b.w[1]), "l"(b.w[2]), "l"(b.w[3]));
+#else
+  uint64_t br = 0;
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t d = a.w[i] - b.w[i];
+    const uint64_t b1 = a.w[i] < b.w[i];
+    r.w[i] = d - br;
+    br = b1 | (d < br);
+  }
+#endif
+  return r;
+}
+
+BP_HD quire256 q_neg(const quire256& a) { return q_sub(q_zero(), a); }
+
+BP_HD bool q_is_zero(const quire256& q) { return (q.w[0] | q.w[1] | q.w[2] | q.w[3]) == 0; }
+
+BP_HD uint64_t q_word(const quire256& q, int i) {
+  // branch-free word select (avoids local-memory indexing on the device)
+  uint64_t r = 0;
+  r = (i == 0) ? q.w[0] : r;
+  r = (i == 1) ? q.w[1] : r;
+  r = (i == 2) ? q.w[2] : r;
+  r = (i == 3) ? q.w[3] : r;
+  return r;
+}
+
+// Unsigned magnitude value m * 2^sh placed into a quire (0 <= sh, m < 2^63,
+// sh + bitlen(m) <= 255).
+BP_HD quire256 q_from_shifted(uint64_t m, int sh) {
+  const int wi = sh >> 6, o = sh & 63;
+  const uint64_t lo = m << o;
+  const uint64_t hi = o ? (m >> (64 - o)) : 0ull;
+  quire256 r;
+  r.w[0] = (wi == 0) ? lo : 0ull;
+  r.w[1] = (wi == 1) ? lo : ((wi == 0) ? hi : 0ull);
+  r.w[2] = (wi == 2) ? lo : ((wi == 1) ? hi : 0ull);
+  r.w[3] = (wi == 3) ? lo : ((wi == 2) ? hi : 0ull);
+  return r;
+}
+
+// quire256 -> bposit<NBITS> (bposit16_encode.cuh:113-204 truncate,
+// 221-321 RTNE, 333-418 bposit32 truncate; bposit16_reference.py:616-631,
+// 775-794).
+template <int NBITS>
+BP_HD uint32_t from_quire(quire256 q, bool rtne) {
+  if (q_is_zero(q)) return 0u;
+  const bool neg = (q.w[3] >> 63) != 0;
+  if (neg) q = q_neg(q);
+  int msb;
+  if (q.w[3]) msb = 192 + 63 - clz64(q.w[3]);
+  else if (q.w[2]) msb = 128 + 63 - clz64(q.w[2]);
+  else if (q.w[1]) msb = 64 + 63 - clz64(q.w[1]);
+  else msb = 63 - clz64(q.w[0]);
+  // 64-bit window of the bits just below the msb, and the sticky remainder.
+  const int lo = msb - 64;                 // window covers [lo, msb-1]
+  uint64_t win;
+  bool sticky = false;
+  if (lo < 0) {
+    win = q.w[0] << (-lo);
+  } else {
+    const int wi = lo >> 6, b = lo & 63;
+    const uint64_t x0 = q_word(q, wi), x1 = q_word(q, wi + 1);
+    win = b ? ((x0 >> b) | (x1 << (64 - b))) : x0;
+    uint64_t below = 0;
+    for (int j = 0; j < 4; ++j) {
+      const int base = 64 * j;
+      const uint64_t wj = q.w[j];
+      if (lo >= base + 64) below |= wj;
+      else if (lo > base) below |= wj & ((1ull << (lo - base)) - 1ull);
+    }
+    sticky = below != 0;
+  }
+  return apply_sign<NBITS>(encode_field<NBITS>(msb - kQuireFracBits, win, sticky, rtne), neg);
+}
+
+// bposit16 decode: value = (-1)^neg * mant * 2^exp2 (bposit16_reference.py:302-374).
+struct Dec16 {
+  uint32_t mant;   // hidden one included, <= 13 bits
+  int exp2;        // exponent of the mantissa's LSB
+  bool neg;
+  bool zero;
+  bool nar;
+};
+
+BP_HD Dec16 decode16(uint32_t p) {
+  Dec16 d;
+  p &= 0xFFFFu;
+  d.zero = p == 0u;
+  d.nar = p == 0x8000u;
+  d.neg = (p >> 15) != 0;
+  uint32_t rest = p & 0x7FFFu;
+  if (d.neg) rest = (0u - rest) & 0x7FFFu;
+  const uint32_t lead = (rest >> 14) & 1u;
+  const uint32_t x = lead ? (~rest & 0x7FFFu) : rest;
+  const int rs = clz32(x) - 17;            // run length of the regime, 1..15
+  int k, e = 0, fw = 0;
+  uint32_t fb = 0;
+  if (rs >= 15) {
+    k = lead ? 14 : -15;
+  } else {
+    k = lead ? rs - 1 : -rs;
+    const int remaining = 14 - rs;
+    const uint32_t rest2 = rest & ((1u << remaining) - 1u);
+    const int ew = remaining < 3 ? remaining : 3;
+    if (ew > 0) e = (int)(((rest2 >> (remaining - ew)) & ((1u << ew) - 1u)) << (3 - ew));
+    fw = remaining - ew;
+    fb = rest2 & ((1u << fw) - 1u);
+  }
+  d.mant = (1u << fw) | fb;
+  d.exp2 = 8 * k + e - fw;
+  return d;
+}
+
+// bposit16 -> quire256 (bposit16_reference.py:602-609: truncation toward
+// zero below 2^-96; zero and NaR map to 0).
+BP_HD quire256 quire_from_bp16(uint32_t p) {
+  const Dec16 d = decode16(p);
+  if (d.zero || d.nar) return q_zero();
+  int sh = d.exp2 + kQuireFracBits;
+  uint64_t m = d.mant;
+  if (sh < 0) {
+    m = (-sh >= 32) ? 0ull : (m >> (-sh));
+    sh = 0;
+  }
+  const quire256 q = q_from_shifted(m, sh);
+  return d.neg ? q_neg(q) : q;
+}
+
+// Exact binary float (value = m * 2^(e)) -> bposit<NBITS>: the exact
+// rational the float denotes (bposit16_reference.py:485-503 given a Fraction).
+template <int NBITS>
+BP_HD uint32_t from_double(double x, bool rtne) {
+  union { double d; uint64_t u; } v;
+  v.d = x;
+  const bool neg = (v.u >> 63) != 0;
+  const int bexp = (int)((v.u >> 52) & 0x7FF);
+  uint64_t man = v.u & ((1ull << 52) - 1);
+  if (bexp == 0 && man == 0) return 0u;
+  if (bexp == 0x7FF) return 1u << (NBITS - 1);           // inf/nan -> NaR
+  int scale;
+  uint64_t frac;
+  if (bexp == 0) {                                          // subnormal
+    const int lz = clz64(man);
+    scale = -1074 + (63 - lz);
+    frac = (man << lz) << 1;
+  } else {
+    scale = bexp - 1023;
+    frac = man << 12;
+  }
+  return apply_sign<NBITS>(encode_field<NBITS>(scale, frac, false, rtne), neg);
+}
+
+}  // namespace bp

@@ -1,0 +1,481 @@
+// capi.cu -- the extern "C" surface of libmosyne_bposit.so and the per-device
+// library state behind it.
+//
+// The reference's nine exports (libmosyne_bposit.cu:95-495) keep their
+// names, signatures, column-major layouts, return codes and stream
+// behaviour (legacy default stream, no synchronisation).  Their bodies are
+// this build's pipeline: coalesced quantiser -> tcgen05 INT8 GEMM with the
+// dequant fused into the epilogue (no INT32 tensor in HBM, no cuBLASLt).
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "alu.cuh"
+#include "bposit.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "quant.cuh"
+#include "quire.cuh"
+
+#include "_gen/bposit16_tables.inc"  // kBposit16Tables[4][65536], generated at build time
+
+#ifndef MOSYNE_BPOSIT_VERSION
+#define MOSYNE_BPOSIT_VERSION "0.1.0-b200"
+#endif
+
+namespace mb {
+
+namespace {
+DeviceContext g_ctx[kMaxDevices];
+std::mutex g_mu;
+
+// Grow-only device staging for the host-pointer entry points.
+struct HostStage {
+  void* buf[6] = {};
+  size_t bytes[6] = {};
+};
+HostStage g_stage[kMaxDevices];
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return (d >= 0 && d < kMaxDevices) ? d : -1;
+}
+
+void free_ctx(DeviceContext& c) {
+  cudaFree(c.err);
+  cudaFree(c.x_i8);
+  cudaFree(c.x_scale);
+  cudaFree(c.amax);
+  cudaFree(c.partials);
+  cudaFree(c.ticket);
+  cudaFree(c.lut);
+  c = DeviceContext();
+}
+
+int init_device(int d) {
+  DeviceContext& c = g_ctx[d];
+  if (c.ready) return RC_OK;
+  c.device = d;
+  if (cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess)
+    return -1;
+  if (cudaMalloc(&c.err, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&c.ticket, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess) {
+    free_ctx(c);
+    return -2;
+  }
+  if (cudaMemset(c.err, 0, sizeof(int)) != cudaSuccess ||
+      cudaMemset(c.ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemcpy(c.lut, kBposit16Tables, sizeof(kBposit16Tables), cudaMemcpyHostToDevice) !=
+          cudaSuccess) {
+    free_ctx(c);
+    return -3;
+  }
+  c.ready = true;
+  return RC_OK;
+}
+
+}  // namespace
+
+DeviceContext* ctx_current() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  return g_ctx[d].ready ? &g_ctx[d] : nullptr;
+}
+
+DeviceContext* ctx_get_or_init() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_ctx[d].ready && init_device(d) != RC_OK) return nullptr;
+  return &g_ctx[d];
+}
+
+int ensure_scratch(void** ptr, size_t* cur, size_t need) {
+  if (*cur >= need) return 0;
+  if (*ptr) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    *cur = 0;
+  }
+  if (cudaMalloc(ptr, need) != cudaSuccess) return -1;
+  *cur = need;
+  return 0;
+}
+
+namespace {
+
+void* stage_buf(int d, int slot, size_t need) {
+  HostStage& s = g_stage[d];
+  if (ensure_scratch(&s.buf[slot], &s.bytes[slot], need ? need : 1)) return nullptr;
+  return s.buf[slot];
+}
+
+bool dtype_ok(int dt) { return dt == MOSYNE_DT_F32 || dt == MOSYNE_DT_BF16 || dt == MOSYNE_DT_F16; }
+
+}  // namespace
+
+int linear_impl(const void* x, int x_dtype, int M, int K, const int8_t* w_i8,
+                const float* w_scale, int N, void* y, int y_dtype, uint32_t* y_bp32,
+                uint16_t* y_bp16, int flags, cudaStream_t st) {
+  DeviceContext* ctx = ctx_current();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || K <= 0 || N <= 0 || !x || !w_i8 || !dtype_ok(x_dtype)) return RC_BAD_ARG;
+  if (y && (!w_scale || !dtype_ok(y_dtype))) return RC_BAD_ARG;
+  const bool per_tensor = (flags & MOSYNE_X_PER_TENSOR) != 0;
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->x_scale), &ctx->x_scale_bytes,
+                     (size_t)M * sizeof(float)))
+    return RC_ALLOC;
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->x_i8), &ctx->x_i8_bytes,
+                     (size_t)M * (size_t)K))
+    return RC_ALLOC;
+  int rc = quant_activation(ctx, x_dtype, x, M, K, ctx->x_i8, ctx->x_scale,
+                            (flags & MOSYNE_X_ROW_MAJOR) != 0, per_tensor, st);
+  if (rc) return rc == RC_ALLOC ? RC_ALLOC : RC_LAUNCH;
+  EpiParams p;
+  p.M = M;
+  p.N = N;
+  p.xs = ctx->x_scale;
+  p.xs_stride = per_tensor ? 0 : 1;
+  p.ws = w_scale;
+  p.ws_stride = (flags & MOSYNE_WS_SCALAR) ? 0 : 1;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.bp32 = y_bp32;
+  p.bp16 = y_bp16;
+  p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+  p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+  p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  rc = gemm_i8_run(ctx->x_i8, w_i8, K, p, ctx, st);
+  return rc == RC_BAD_ARG ? RC_BAD_ARG : (rc ? RC_GEMM : RC_OK);
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+// ---------------------------------------------------------------- reference ABI
+
+int mosyne_bposit_init(void) {
+  const int d = current_device();
+  if (d < 0) return -1;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return init_device(d);
+}
+
+void mosyne_bposit_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int cur = -1;
+  cudaGetDevice(&cur);
+  for (int d = 0; d < kMaxDevices; ++d) {
+    const bool has_stage = g_stage[d].buf[0] || g_stage[d].buf[1] || g_stage[d].buf[2] ||
+                           g_stage[d].buf[3] || g_stage[d].buf[4] || g_stage[d].buf[5];
+    if (!g_ctx[d].ready && !has_stage) continue;
+    cudaSetDevice(d);
+    free_ctx(g_ctx[d]);
+    for (int i = 0; i < 6; ++i) {
+      cudaFree(g_stage[d].buf[i]);
+      g_stage[d].buf[i] = nullptr;
+      g_stage[d].bytes[i] = 0;
+    }
+  }
+  if (cur >= 0) cudaSetDevice(cur);
+}
+
+int mosyne_bposit_quantize_weight_per_channel(const float* w_fp32, int K, int N, int8_t* w_i8_out,
+                                              float* w_scale_out) {
+  if (K <= 0 || N <= 0 || !w_fp32 || !w_i8_out || !w_scale_out) return RC_LAUNCH;
+  return quant_rows(MOSYNE_DT_F32, w_fp32, N, K, w_i8_out, w_scale_out, 0) ? RC_LAUNCH : RC_OK;
+}
+
+int mosyne_bposit_linear_w8a8(const float* x, int M, int K, const int8_t* w_i8,
+                              const float* w_scale, int N, float* y) {
+  return linear_impl(x, MOSYNE_DT_F32, M, K, w_i8, w_scale, N, y, MOSYNE_DT_F32, nullptr,
+                     nullptr, 0, 0);
+}
+
+int mosyne_bposit_linear_w8a8_bf16(const mosyne_bf16_t* x, int M, int K, const int8_t* w_i8,
+                                   const float* w_scale, int N, float* y) {
+  return linear_impl(x, MOSYNE_DT_BF16, M, K, w_i8, w_scale, N, y, MOSYNE_DT_F32, nullptr,
+                     nullptr, 0, 0);
+}
+
+int mosyne_bposit_linear_w8a8_bf16_io(const mosyne_bf16_t* x, int M, int K, const int8_t* w_i8,
+                                      const float* w_scale, int N, mosyne_bf16_t* y) {
+  return linear_impl(x, MOSYNE_DT_BF16, M, K, w_i8, w_scale, N, y, MOSYNE_DT_BF16, nullptr,
+                     nullptr, 0, 0);
+}
+
+int mosyne_bposit_linear_w8a8_fp16(const mosyne_fp16_t* x, int M, int K, const int8_t* w_i8,
+                                   const float* w_scale, int N, float* y) {
+  return linear_impl(x, MOSYNE_DT_F16, M, K, w_i8, w_scale, N, y, MOSYNE_DT_F32, nullptr,
+                     nullptr, 0, 0);
+}
+
+int mosyne_bposit_linear_w8a8_fp16_io(const mosyne_fp16_t* x, int M, int K, const int8_t* w_i8,
+                                      const float* w_scale, int N, mosyne_fp16_t* y) {
+  return linear_impl(x, MOSYNE_DT_F16, M, K, w_i8, w_scale, N, y, MOSYNE_DT_F16, nullptr,
+                     nullptr, 0, 0);
+}
+
+int mosyne_bposit_linear_w8a8_host(const float* host_x, int M, int K, const float* host_w, int N,
+                                   float* host_y) {
+  if (!ctx_current()) {
+    const int rc = mosyne_bposit_init();
+    if (rc != 0) return rc;
+  }
+  if (M <= 0 || K <= 0 || N <= 0 || !host_x || !host_w || !host_y) return RC_BAD_ARG;
+  const int d = current_device();
+  float* dx = static_cast<float*>(stage_buf(d, 0, (size_t)M * K * sizeof(float)));
+  float* dw = static_cast<float*>(stage_buf(d, 1, (size_t)K * N * sizeof(float)));
+  float* dy = static_cast<float*>(stage_buf(d, 2, (size_t)M * N * sizeof(float)));
+  int8_t* dwi8 = static_cast<int8_t*>(stage_buf(d, 3, (size_t)K * N));
+  float* dws = static_cast<float*>(stage_buf(d, 4, (size_t)N * sizeof(float)));
+  if (!dx || !dw || !dy || !dwi8 || !dws) return RC_ALLOC;
+  if (cudaMemcpy(dx, host_x, (size_t)M * K * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(dw, host_w, (size_t)K * N * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+    return RC_LAUNCH;
+  int rc = mosyne_bposit_quantize_weight_per_channel(dw, K, N, dwi8, dws);
+  if (rc == 0) rc = mosyne_bposit_linear_w8a8(dx, M, K, dwi8, dws, N, dy);
+  if (rc == 0 && cudaMemcpy(host_y, dy, (size_t)M * N * sizeof(float), cudaMemcpyDeviceToHost) !=
+                     cudaSuccess)
+    rc = RC_LAUNCH;
+  return rc;
+}
+
+// ---------------------------------------------------------------- additions
+
+const char* mosyne_bposit_version(void) { return MOSYNE_BPOSIT_VERSION " sm_100a tcgen05"; }
+
+int mosyne_bposit_last_error(void) {
+  DeviceContext* ctx = ctx_current();
+  if (cudaDeviceSynchronize() != cudaSuccess) return RC_LAUNCH;
+  if (!ctx) return RC_OK;
+  int h = 0;
+  if (cudaMemcpy(&h, ctx->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return RC_LAUNCH;
+  if (h != 0) {
+    cudaMemset(ctx->err, 0, sizeof(int));
+    return RC_DEVICE_TIMEOUT;
+  }
+  return RC_OK;
+}
+
+int mosyne_bposit_debug_wait_timeout(unsigned long long limit_ns, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  return debug_wait_run(limit_ns, ctx, as_stream(stream));
+}
+
+int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
+                          const float* x_scale, const float* w_scale, uint32_t* out_bp32,
+                          uint16_t* out_bp16, void* out_y, int y_dtype, int32_t* out_i32,
+                          int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return RC_BAD_ARG;
+  if (out_y && (!x_scale || !w_scale || !dtype_ok(y_dtype))) return RC_BAD_ARG;
+  EpiParams p;
+  p.M = M;
+  p.N = N;
+  p.xs = x_scale;
+  p.ws = w_scale;
+  p.xs_stride = (flags & MOSYNE_XS_SCALAR) ? 0 : 1;
+  p.ws_stride = (flags & MOSYNE_WS_SCALAR) ? 0 : 1;
+  p.bp32 = out_bp32;
+  p.bp16 = out_bp16;
+  p.y = out_y;
+  p.y_dtype = y_dtype;
+  p.i32 = out_i32;
+  p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+  p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+  p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  const int path = (flags >> 16) & 0xF;  // test hook: force a GEMM path
+  return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
+}
+
+int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, int K,
+                               uint32_t* out_bp32, int32_t* out_i32, int flags) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return RC_BAD_ARG;
+  const int d = ctx->device;
+  const size_t mk = (size_t)M * K, nk = (size_t)N * K, mn = (size_t)M * N;
+  int8_t* dA = static_cast<int8_t*>(stage_buf(d, 0, mk));
+  int8_t* dB = static_cast<int8_t*>(stage_buf(d, 1, nk));
+  uint32_t* dbp = out_bp32 ? static_cast<uint32_t*>(stage_buf(d, 2, mn * 4)) : nullptr;
+  int32_t* di = out_i32 ? static_cast<int32_t*>(stage_buf(d, 3, mn * 4)) : nullptr;
+  if (!dA || !dB || (out_bp32 && !dbp) || (out_i32 && !di)) return RC_ALLOC;
+  cudaStream_t st = 0;
+  if (cudaMemcpyAsync(dA, A, mk, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(dB, B, nk, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return RC_LAUNCH;
+  int rc = mosyne_bposit_gemm_i8(dA, dB, M, N, K, nullptr, nullptr, dbp, nullptr, nullptr,
+                                 MOSYNE_DT_F32, di, flags & ~(MOSYNE_XS_SCALAR | MOSYNE_WS_SCALAR),
+                                 nullptr);
+  if (rc) return rc;
+  if (dbp && cudaMemcpyAsync(out_bp32, dbp, mn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return RC_LAUNCH;
+  if (di && cudaMemcpyAsync(out_i32, di, mn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return RC_LAUNCH;
+  return cudaStreamSynchronize(st) == cudaSuccess ? RC_OK : RC_LAUNCH;
+}
+
+int mosyne_bposit_linear_w8a8_ex(const void* x, int x_dtype, int M, int K, const int8_t* w_i8,
+                                 const float* w_scale, int N, void* y, int y_dtype,
+                                 uint32_t* y_bp32, uint16_t* y_bp16, int flags,
+                                 mosyne_stream_t stream) {
+  return linear_impl(x, x_dtype, M, K, w_i8, w_scale, N, y, y_dtype, y_bp32, y_bp16, flags,
+                     as_stream(stream));
+}
+
+int mosyne_bposit_quantize_per_token(const void* x, int x_dtype, int M, int K, int8_t* x_i8,
+                                     float* x_scale, int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || K <= 0 || !x || !x_i8 || !dtype_ok(x_dtype)) return RC_BAD_ARG;
+  return quant_activation(ctx, x_dtype, x, M, K, x_i8, x_scale, (flags & MOSYNE_X_ROW_MAJOR) != 0,
+                          false, as_stream(stream));
+}
+
+int mosyne_bposit_quantize_per_tensor(const void* t, int dtype, int rows, int cols, int8_t* q,
+                                      float* scale, int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (rows <= 0 || cols <= 0 || !t || !q || !dtype_ok(dtype)) return RC_BAD_ARG;
+  return quant_activation(ctx, dtype, t, rows, cols, q, scale, (flags & MOSYNE_X_ROW_MAJOR) != 0,
+                          true, as_stream(stream));
+}
+
+int mosyne_bposit_quantize_weight_per_channel_ex(const void* w, int dtype, int K, int N,
+                                                 int8_t* w_i8_out, float* w_scale_out,
+                                                 mosyne_stream_t stream) {
+  if (K <= 0 || N <= 0 || !w || !w_i8_out || !w_scale_out || !dtype_ok(dtype)) return RC_BAD_ARG;
+  return quant_rows(dtype, w, N, K, w_i8_out, w_scale_out, as_stream(stream));
+}
+
+int mosyne_bposit_quire_sum_bp16(const uint16_t* x, size_t n, mosyne_quire256* q_out,
+                                 uint16_t* bp16_out, uint32_t* bp32_out, int flags,
+                                 mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  return quire_sum_bp16_run(ctx, x, n, q_out, bp16_out, bp32_out, flags, as_stream(stream),
+                            (flags >> 16) & 0xFFFF);
+}
+
+int mosyne_bposit_fp32_atomic_sum(const float* x, size_t n, float* acc, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (!acc || (n && !x)) return RC_BAD_ARG;
+  return fp32_atomic_sum_run(ctx, x, n, acc, as_stream(stream));
+}
+
+int mosyne_bposit_quire_to_bp16(const mosyne_quire256* q, size_t n, uint16_t* out, int rtne,
+                                mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (n && (!q || !out)) return RC_BAD_ARG;
+  return quire_to_bp_run(ctx, q, n, out, 16, rtne, as_stream(stream));
+}
+
+int mosyne_bposit_quire_to_bp32(const mosyne_quire256* q, size_t n, uint32_t* out, int rtne,
+                                mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (n && (!q || !out)) return RC_BAD_ARG;
+  return quire_to_bp_run(ctx, q, n, out, 32, rtne, as_stream(stream));
+}
+
+int mosyne_bposit_bp16_to_quire(const uint16_t* x, size_t n, mosyne_quire256* out,
+                                mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (n && (!x || !out)) return RC_BAD_ARG;
+  return bp16_to_quire_run(ctx, x, n, out, as_stream(stream));
+}
+
+int mosyne_bposit_int32_to_bp32(const int32_t* in, size_t n, int scale_shift, uint32_t* out,
+                                int rtne, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (n && (!in || !out)) return RC_BAD_ARG;
+  return int32_to_bp32_run(ctx, in, n, scale_shift, out, rtne, as_stream(stream));
+}
+
+int mosyne_bposit_float_to_bposit(const void* x, int dtype, size_t n, void* out, int nbits,
+                                  int rtne, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if ((n && (!x || !out)) || (nbits != 16 && nbits != 32)) return RC_BAD_ARG;
+  return float_to_bposit_run(ctx, x, dtype, n, out, nbits, rtne, as_stream(stream));
+}
+
+int mosyne_bposit_epilogue_i32(const int32_t* acc, int M, int N, const float* x_scale,
+                               const float* w_scale, uint32_t* out_bp32, uint16_t* out_bp16,
+                               void* out_y, int y_dtype, int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || N <= 0 || !acc) return RC_BAD_ARG;
+  if (out_y && (!x_scale || !w_scale || !dtype_ok(y_dtype))) return RC_BAD_ARG;
+  EpiParams p;
+  p.M = M;
+  p.N = N;
+  p.xs = x_scale;
+  p.ws = w_scale;
+  p.xs_stride = (flags & MOSYNE_XS_SCALAR) ? 0 : 1;
+  p.ws_stride = (flags & MOSYNE_WS_SCALAR) ? 0 : 1;
+  p.bp32 = out_bp32;
+  p.bp16 = out_bp16;
+  p.y = out_y;
+  p.y_dtype = y_dtype;
+  p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+  p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+  p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  return epilogue_i32_run(acc, p, ctx, as_stream(stream));
+}
+
+#define MB_ALU_ENTRY(name, op)                                                           \
+  int name(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream) {         \
+    DeviceContext* ctx = ctx_get_or_init();                                              \
+    if (!ctx) return RC_NOT_INIT;                                                        \
+    return alu_run(ctx, op, a, nullptr, n, out, as_stream(stream));                      \
+  }
+#define MB_ALU_ENTRY2(name, op)                                                          \
+  int name(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out,               \
+           mosyne_stream_t stream) {                                                     \
+    DeviceContext* ctx = ctx_get_or_init();                                              \
+    if (!ctx) return RC_NOT_INIT;                                                        \
+    if (n && !b) return RC_BAD_ARG;                                                      \
+    return alu_run(ctx, op, a, b, n, out, as_stream(stream));                            \
+  }
+
+MB_ALU_ENTRY2(mosyne_bposit16_add, ALU_ADD)
+MB_ALU_ENTRY2(mosyne_bposit16_mul, ALU_MUL)
+MB_ALU_ENTRY2(mosyne_bposit16_mul_exact, ALU_MUL_EXACT)
+MB_ALU_ENTRY(mosyne_bposit16_recip, ALU_RECIP)
+MB_ALU_ENTRY(mosyne_bposit16_sqrt, ALU_SQRT)
+MB_ALU_ENTRY(mosyne_bposit16_log2, ALU_LOG2)
+MB_ALU_ENTRY(mosyne_bposit16_exp2, ALU_EXP2)
+
+int mosyne_bposit16_neg(const uint16_t* a, size_t n, uint16_t* out, int ones_complement,
+                        mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  return alu_run(ctx, ones_complement ? ALU_NEG_ONES : ALU_NEG, a, nullptr, n, out,
+                 as_stream(stream));
+}
+
+int mosyne_bposit16_table_host(int which, uint16_t* host_out) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (which < 0 || which >= MB_LUT_COUNT || !host_out) return RC_BAD_ARG;
+  return cudaMemcpy(host_out, ctx->lut + (size_t)which * 65536, 65536 * sizeof(uint16_t),
+                    cudaMemcpyDeviceToHost) == cudaSuccess
+             ? RC_OK
+             : RC_LAUNCH;
+}
+
+}  // extern "C"

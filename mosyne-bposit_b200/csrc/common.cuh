@@ -1,0 +1,98 @@
+// common.cuh -- library-wide state, error codes and small device helpers.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/mosyne_bposit.h"
+
+namespace mb {
+
+// Per-device library state.  The reference keeps one process-global state for
+// the device current at init (libmosyne_bposit.cu:49-77); this build keeps
+// one context per device ordinal so multi-GPU processes work.
+struct DeviceContext {
+  bool ready = false;
+  int device = -1;
+  int num_sms = 0;
+  int* err = nullptr;              // device error word (first failure code)
+  // grow-only scratch for the W8A8 path (libmosyne_bposit.cu:56-61)
+  int8_t* x_i8 = nullptr;
+  size_t x_i8_bytes = 0;
+  float* x_scale = nullptr;
+  size_t x_scale_bytes = 0;
+  uint32_t* amax = nullptr;        // per-row / per-tensor |max| bit patterns
+  size_t amax_bytes = 0;
+  void* partials = nullptr;        // exact-sum block partials
+  size_t partials_bytes = 0;
+  unsigned int* ticket = nullptr;  // last-block ticket for grid reductions
+  // bposit16 ALU tables, 65,536 x u16 each, device resident
+  uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]
+};
+
+enum LutId { LUT_LOG2 = 0, LUT_EXP2 = 1, LUT_SQRT = 2, LUT_RECIP = 3, MB_LUT_COUNT = 4 };
+
+constexpr int kMaxDevices = 64;
+
+DeviceContext* ctx_current();       // context of the current device, or nullptr
+DeviceContext* ctx_get_or_init();   // initialise lazily (for the new entry points)
+int ensure_scratch(void** ptr, size_t* cur, size_t need);
+
+// error codes (reference: libmosyne_bposit.cu:95-143, 322-348)
+constexpr int RC_OK = 0;
+constexpr int RC_LAUNCH = -1;
+constexpr int RC_GEMM = -2;
+constexpr int RC_NOT_INIT = -10;
+constexpr int RC_ALLOC = -11;
+constexpr int RC_BAD_ARG = -20;
+constexpr int RC_DEVICE_TIMEOUT = -30;
+
+// device error-word codes (which wait gave up)
+constexpr int ERR_PRODUCER_WAIT = 1;
+constexpr int ERR_MMA_WAIT_FULL = 2;
+constexpr int ERR_MMA_WAIT_TMEM = 3;
+constexpr int ERR_EPI_WAIT = 4;
+constexpr int ERR_DRAIN_WAIT = 5;
+constexpr int ERR_TEST_WAIT = 6;
+
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+inline cudaStream_t as_stream(mosyne_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int launch_rc() { return cudaGetLastError() == cudaSuccess ? RC_OK : RC_LAUNCH; }
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+// 127 / max in fp32, 1.0 for an all-zero slice (libmosyne_bposit.cu:170, 234).
+__device__ __forceinline__ float quant_scale_from_max(float amax) {
+  return (amax > 1e-8f) ? __fdiv_rn(127.f, amax) : 1.f;
+}
+
+// rint(clamp(v*s, +-127)) (libmosyne_bposit.cu:178-180, 240-242).
+__device__ __forceinline__ int8_t quantize1(float v, float s) {
+  float t = __fmul_rn(v, s);
+  t = fminf(127.f, fmaxf(-127.f, t));
+  return (int8_t)__float2int_rn(t);
+}
+
+// Wall-clock bound for every device-side wait (ns).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+}  // namespace mb

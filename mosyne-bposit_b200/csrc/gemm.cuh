@@ -1,0 +1,46 @@
+// gemm.cuh -- fused INT8 GEMM / epilogue interface shared by the C ABI.
+#pragma once
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace mb {
+
+// Outputs of the fused epilogue for acc[m,n] (exact INT32):
+//   bp32 = bposit32(acc), bp16 = bposit16(acc), i32 = acc,
+//   y    = (float)acc / (xs[m*xs_stride] * ws[n*ws_stride]) in y_dtype.
+// Null pointers are skipped.  Index: row_major ? m*N + n : n*M + m.
+struct EpiParams {
+  int M = 0, N = 0;
+  const float* xs = nullptr;
+  const float* ws = nullptr;
+  int xs_stride = 1, ws_stride = 1;
+  uint32_t* bp32 = nullptr;
+  uint16_t* bp16 = nullptr;
+  void* y = nullptr;
+  int y_dtype = MOSYNE_DT_F32;
+  int32_t* i32 = nullptr;
+  int row_major = 0;
+  int rtne32 = 0, rtne16 = 0;
+};
+
+enum GemmPath {
+  GEMM_PATH_AUTO = 0,
+  GEMM_PATH_TC = 1,        // tensor-core path, tile width chosen by shape
+  GEMM_PATH_TC_BN128 = 2,
+  GEMM_PATH_TC_BN256 = 3,
+  GEMM_PATH_SIMT = 4,
+};
+
+// acc = A[M,K] (K contiguous) x B[N,K]^T (K contiguous), fused epilogue.
+int gemm_i8_run(const int8_t* A, const int8_t* B, int K, const EpiParams& p,
+                DeviceContext* ctx, cudaStream_t st, int force_path = GEMM_PATH_AUTO);
+
+// Same epilogue over a column-major INT32 accumulator.
+int epilogue_i32_run(const int32_t* acc, const EpiParams& p, DeviceContext* ctx,
+                     cudaStream_t st);
+
+// Bounded wait that nothing satisfies; sets the device error word.
+int debug_wait_run(unsigned long long limit_ns, DeviceContext* ctx, cudaStream_t st);
+
+}  // namespace mb

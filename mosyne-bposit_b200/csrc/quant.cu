@@ -1,0 +1,287 @@
+// quant.cu -- symmetric int8 quantisers (per-channel, per-token, per-tensor).
+//
+// Arithmetic is the reference's, bit for bit (libmosyne_bposit.cu:162-244):
+// scale = 127.f / max|slice| (1.0 when max <= 1e-8), q = rint(clamp(v*scale,
+// +-127)).  The layouts differ from the reference on purpose: activations
+// always leave here K-contiguous ([M,K] row-major), the operand layout the
+// tensor-core GEMM's TMA loads, and every read is coalesced (the reference's
+// per-token kernel walks column-major x with stride M, libmosyne_bposit.cu:218).
+#include "common.cuh"
+#include "quant.cuh"
+
+namespace mb {
+namespace {
+
+template <typename T>
+struct Vec;  // 16-byte vectors
+template <>
+struct Vec<float> {
+  static constexpr int N = 4;
+};
+template <>
+struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+};
+template <>
+struct Vec<__half> {
+  static constexpr int N = 8;
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per contiguous row: max over the row, then quantise it.  Used for
+// per-channel weights (column-major [K,N] = N contiguous rows of K) and for
+// row-major activations.  `given_amax` (nullable) supplies a per-tensor max.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x, int R, int C,
+                                                         int8_t* __restrict__ q,
+                                                         float* __restrict__ scale,
+                                                         const uint32_t* __restrict__ given_amax) {
+  constexpr int V = Vec<T>::N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= R) return;
+  const T* xr = x + (size_t)row * C;
+  int8_t* qr = q + (size_t)row * C;
+  float m = 0.f;
+  if (given_amax) {
+    m = __uint_as_float(*given_amax);
+  } else {
+    if (VEC) {
+      for (int c = lane * V; c < C; c += 32 * V) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+        const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32<T>(v[i])));
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) m = fmaxf(m, fabsf(to_f32<T>(xr[c])));
+    }
+    m = warp_max(m);
+  }
+  const float s = quant_scale_from_max(m);
+  if (lane == 0 && scale) scale[row] = s;
+  if (VEC) {
+    for (int c = lane * V; c < C; c += 32 * V) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+      const T* v = reinterpret_cast<const T*>(&raw);
+      int8_t o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = quantize1(to_f32<T>(v[i]), s);
+      if (V == 4) {
+        *reinterpret_cast<uint32_t*>(qr + c) = *reinterpret_cast<uint32_t*>(o);
+      } else {
+        *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<uint2*>(o);
+      }
+    }
+  } else {
+    for (int c = lane; c < C; c += 32) qr[c] = quantize1(to_f32<T>(xr[c]), s);
+  }
+}
+
+// Column-major x [M,K] (m contiguous): per-row |max| via coalesced reads of
+// 64 consecutive rows, reduced with atomicMax on the fp32 bit pattern (exact
+// and order independent for non-negative values).
+template <typename T>
+__global__ void __launch_bounds__(256) colmajor_rowmax_kernel(const T* __restrict__ x, int M,
+                                                              int K, int k_chunk,
+                                                              uint32_t* __restrict__ amax) {
+  __shared__ float red[4][64];
+  const int ml = threadIdx.x & 63, kl = threadIdx.x >> 6;
+  const int m = blockIdx.x * 64 + ml;
+  const int k_begin = blockIdx.y * k_chunk;
+  const int k_end = min(K, k_begin + k_chunk);
+  float v = 0.f;
+  if (m < M) {
+    for (int k = k_begin + kl; k < k_end; k += 4) v = fmaxf(v, fabsf(to_f32<T>(x[(size_t)k * M + m])));
+  }
+  red[kl][ml] = v;
+  __syncthreads();
+  if (kl == 0 && m < M) {
+    v = fmaxf(fmaxf(red[0][ml], red[1][ml]), fmaxf(red[2][ml], red[3][ml]));
+    atomicMax(&amax[m], __float_as_uint(v));
+  }
+}
+
+// Column-major x [M,K] -> int8 [M,K] row-major through a 64x64 shared tile.
+// amax_stride = 1: per-row max (per token); 0: one max (per tensor).
+template <typename T>
+__global__ void __launch_bounds__(256) colmajor_quant_kernel(const T* __restrict__ x, int M,
+                                                             int K,
+                                                             const uint32_t* __restrict__ amax,
+                                                             int amax_stride,
+                                                             int8_t* __restrict__ q,
+                                                             float* __restrict__ scale) {
+  __shared__ __align__(16) int8_t tile[64][64 + 16];
+  __shared__ float srow[64];
+  const int m0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
+  const int ml = threadIdx.x & 63, kl = threadIdx.x >> 6;
+  if (threadIdx.x < 64) {
+    const int m = m0 + threadIdx.x;
+    const float s = m < M ? quant_scale_from_max(__uint_as_float(amax[(size_t)m * amax_stride])) : 1.f;
+    srow[threadIdx.x] = s;
+    if (scale && blockIdx.y == 0 && m < M && (amax_stride || m == 0)) scale[m] = s;
+  }
+  __syncthreads();
+  const int m = m0 + ml;
+  const float s = srow[ml];
+#pragma unroll 4
+  for (int kk = kl; kk < 64; kk += 4) {
+    const int k = k0 + kk;
+    int8_t v = 0;
+    if (m < M && k < K) v = quantize1(to_f32<T>(x[(size_t)k * M + m]), s);
+    tile[ml][kk] = v;
+  }
+  __syncthreads();
+  // 64 rows x 4 chunks of 16 bytes
+  const int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 16;
+  const int mo = m0 + r;
+  if (mo < M) {
+    int8_t* dst = q + (size_t)mo * K + k0 + c;
+    if (((K & 15) == 0) && (k0 + c + 16 <= K)) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&tile[r][c]);
+    } else {
+      for (int i = 0; i < 16 && k0 + c + i < K; ++i) dst[i] = tile[r][c + i];
+    }
+  }
+}
+
+template <typename T, int V>
+__global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, size_t n,
+                                                     uint32_t* __restrict__ amax) {
+  __shared__ float red[8];
+  float m = 0.f;
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  if (V > 1) {
+    const size_t nv = n / V;
+    for (size_t i = tid; i < nv; i += stride) {
+      const uint4 raw = reinterpret_cast<const uint4*>(x)[i];
+      const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32<T>(v[j])));
+    }
+    for (size_t i = nv * V + tid; i < n; i += stride) m = fmaxf(m, fabsf(to_f32<T>(x[i])));
+  } else {
+    for (size_t i = tid; i < n; i += stride) m = fmaxf(m, fabsf(to_f32<T>(x[i])));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    m = warp_max(m);
+    if (threadIdx.x == 0) atomicMax(amax, __float_as_uint(m));
+  }
+}
+
+template <typename T>
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+template <typename T>
+int quant_rows_t(const void* x, int R, int C, int8_t* q, float* scale, const uint32_t* amax,
+                 cudaStream_t st) {
+  constexpr int V = Vec<T>::N;
+  const bool vec = (C % V == 0) && aligned16<T>(x) && ((reinterpret_cast<uintptr_t>(q) % V) == 0);
+  const unsigned blocks = (unsigned)((R + 7) / 8);
+  if (vec)
+    quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax);
+  else
+    quant_rows_kernel<T, false><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax);
+  return launch_rc();
+}
+
+template <typename T>
+int colmajor_per_token_t(DeviceContext* ctx, const void* x, int M, int K, int8_t* q,
+                         float* scale, cudaStream_t st) {
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->amax), &ctx->amax_bytes,
+                     (size_t)M * sizeof(uint32_t)))
+    return RC_ALLOC;
+  cudaMemsetAsync(ctx->amax, 0, (size_t)M * sizeof(uint32_t), st);
+  const int gm = (M + 63) / 64;
+  int splits = (2 * ctx->num_sms + gm - 1) / gm;
+  splits = max(1, min(splits, (K + 63) / 64));
+  const int k_chunk = (K + splits - 1) / splits;
+  colmajor_rowmax_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
+      static_cast<const T*>(x), M, K, k_chunk, ctx->amax);
+  colmajor_quant_kernel<T><<<dim3(gm, (K + 63) / 64), 256, 0, st>>>(static_cast<const T*>(x), M, K,
+                                                                    ctx->amax, 1, q, scale);
+  return launch_rc();
+}
+
+template <typename T>
+int per_tensor_t(DeviceContext* ctx, const void* t, int rows, int cols, int8_t* q, float* scale,
+                 bool row_major, cudaStream_t st) {
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->amax), &ctx->amax_bytes, sizeof(uint32_t)))
+    return RC_ALLOC;
+  cudaMemsetAsync(ctx->amax, 0, sizeof(uint32_t), st);
+  const size_t n = (size_t)rows * (size_t)cols;
+  size_t nb = (n + 2047) / 2048;
+  if (nb > (size_t)ctx->num_sms * 4) nb = (size_t)ctx->num_sms * 4;
+  unsigned blocks = (unsigned)nb;
+  if (blocks == 0) blocks = 1;
+  if (aligned16<T>(t))
+    absmax_kernel<T, Vec<T>::N><<<blocks, 256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
+  else
+    absmax_kernel<T, 1><<<blocks, 256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
+  int rc = launch_rc();
+  if (rc) return rc;
+  if (row_major) {
+    rc = quant_rows_t<T>(t, rows, cols, q, nullptr, ctx->amax, st);
+    if (rc) return rc;
+    return write_scalar_scale(ctx->amax, scale, st);
+  }
+  colmajor_quant_kernel<T><<<dim3((rows + 63) / 64, (cols + 63) / 64), 256, 0, st>>>(
+      static_cast<const T*>(t), rows, cols, ctx->amax, 0, q, scale);
+  return launch_rc();
+}
+
+__global__ void scalar_scale_kernel(const uint32_t* amax, float* scale) {
+  *scale = quant_scale_from_max(__uint_as_float(*amax));
+}
+
+}  // namespace
+
+int write_scalar_scale(const uint32_t* amax, float* scale, cudaStream_t st) {
+  if (!scale) return RC_OK;
+  scalar_scale_kernel<<<1, 1, 0, st>>>(amax, scale);
+  return launch_rc();
+}
+
+int quant_rows(int dtype, const void* x, int R, int C, int8_t* q, float* scale, cudaStream_t st) {
+  if (R <= 0 || C <= 0) return R == 0 || C == 0 ? RC_OK : RC_BAD_ARG;
+  switch (dtype) {
+    case MOSYNE_DT_F32: return quant_rows_t<float>(x, R, C, q, scale, nullptr, st);
+    case MOSYNE_DT_BF16: return quant_rows_t<__nv_bfloat16>(x, R, C, q, scale, nullptr, st);
+    case MOSYNE_DT_F16: return quant_rows_t<__half>(x, R, C, q, scale, nullptr, st);
+    default: return RC_BAD_ARG;
+  }
+}
+
+int quant_activation(DeviceContext* ctx, int dtype, const void* x, int M, int K, int8_t* q,
+                     float* scale, bool row_major, bool per_tensor, cudaStream_t st) {
+  if (M <= 0 || K <= 0) return RC_BAD_ARG;
+  if (per_tensor) {
+    switch (dtype) {
+      case MOSYNE_DT_F32: return per_tensor_t<float>(ctx, x, M, K, q, scale, row_major, st);
+      case MOSYNE_DT_BF16: return per_tensor_t<__nv_bfloat16>(ctx, x, M, K, q, scale, row_major, st);
+      case MOSYNE_DT_F16: return per_tensor_t<__half>(ctx, x, M, K, q, scale, row_major, st);
+      default: return RC_BAD_ARG;
+    }
+  }
+  if (row_major) return quant_rows(dtype, x, M, K, q, scale, st);
+  switch (dtype) {
+    case MOSYNE_DT_F32: return colmajor_per_token_t<float>(ctx, x, M, K, q, scale, st);
+    case MOSYNE_DT_BF16: return colmajor_per_token_t<__nv_bfloat16>(ctx, x, M, K, q, scale, st);
+    case MOSYNE_DT_F16: return colmajor_per_token_t<__half>(ctx, x, M, K, q, scale, st);
+    default: return RC_BAD_ARG;
+  }
+}
+
+}  // namespace mb

@@ -1,0 +1,18 @@
+// quant.cuh -- quantiser entry points used by the C ABI.
+#pragma once
+#include "common.cuh"
+
+namespace mb {
+
+// Contiguous rows [R, C] -> int8 [R, C] with one scale per row
+// (per-channel weights: R = N, C = K of a column-major [K,N] weight).
+int quant_rows(int dtype, const void* x, int R, int C, int8_t* q, float* scale, cudaStream_t st);
+
+// Activation x [M,K] (column-major, or row-major) -> int8 [M,K] row-major
+// (K contiguous) with per-token scales x_scale[M] or one per-tensor scale.
+int quant_activation(DeviceContext* ctx, int dtype, const void* x, int M, int K, int8_t* q,
+                     float* scale, bool row_major, bool per_tensor, cudaStream_t st);
+
+int write_scalar_scale(const uint32_t* amax, float* scale, cudaStream_t st);
+
+}  // namespace mb

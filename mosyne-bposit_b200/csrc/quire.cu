@@ -1,0 +1,235 @@
+// quire.cu -- exact quire256 reductions and element-wise bposit conversions.
+//
+// The exact sum replaces the reference's single-warp reduction
+// (kernels/test_determinism_headline.cu:65-91, <<<1,32>>>, which is only
+// correct for one warp) and the <=32-block entropy reduction
+// (kernels/shannon_entropy_bposit16.cu:45-119) with a grid-wide one:
+// 16-byte loads of 8 codes, arithmetic bposit16 -> fixed-point decode
+// (no 2 MiB table), a per-thread 256-bit accumulator updated with add.cc
+// chains, warp shuffles, a shared-memory block step, per-block partials and
+// a last-block finish.  Integer addition is associative, so the quire (and
+// every encoding of it) is identical for any grid, schedule or GPU.
+#include "bposit.cuh"
+#include "common.cuh"
+#include "quire.cuh"
+
+namespace mb {
+namespace {
+
+using bp::quire256;
+
+__device__ __forceinline__ void q_accumulate_bp16(quire256& acc, uint32_t code) {
+  const bp::Dec16 d = bp::decode16(code);
+  if (d.zero || d.nar) return;
+  int sh = d.exp2 + bp::kQuireFracBits;
+  uint64_t m = d.mant;
+  if (sh < 0) {
+    m = (-sh >= 32) ? 0ull : (m >> (-sh));
+    sh = 0;
+  }
+  const quire256 t = bp::q_from_shifted(m, sh);
+  acc = d.neg ? bp::q_sub(acc, t) : bp::q_add(acc, t);
+}
+
+__device__ __forceinline__ quire256 shfl_down_q(const quire256& q, int off) {
+  quire256 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r.w[i] = __shfl_down_sync(0xffffffffu, q.w[i], off);
+  return r;
+}
+
+__device__ __forceinline__ quire256 block_reduce_q(quire256 q, quire256* sh /*[32]*/) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) q = bp::q_add(q, shfl_down_q(q, off));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = q;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  if (warp == 0) {
+    q = lane < nw ? sh[lane] : bp::q_zero();
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q = bp::q_add(q, shfl_down_q(q, off));
+  }
+  return q;  // valid in thread 0
+}
+
+__global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
+    const uint16_t* __restrict__ x, size_t n, quire256* __restrict__ partials,
+    unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
+    uint32_t* bp32_out, int rtne16, int rtne32) {
+  __shared__ quire256 sh[32];
+  __shared__ bool is_last;
+  quire256 acc = bp::q_zero();
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  size_t done = 0;
+  if (vec) {
+    const size_t nv = n / 8;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (size_t i = tid; i < nv; i += stride) {
+      const uint4 r = __ldg(xv + i);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        q_accumulate_bp16(acc, w[j] & 0xFFFFu);
+        q_accumulate_bp16(acc, w[j] >> 16);
+      }
+    }
+    done = nv * 8;
+  }
+  for (size_t i = done + tid; i < n; i += stride) q_accumulate_bp16(acc, x[i]);
+
+  acc = block_reduce_q(acc, sh);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = acc;
+    __threadfence();
+    const unsigned int t = atomicAdd(ticket, 1u);
+    is_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  quire256 q = bp::q_zero();
+  for (unsigned int i = threadIdx.x; i < gridDim.x; i += blockDim.x) {
+    const volatile uint64_t* pw = reinterpret_cast<volatile uint64_t*>(&partials[i]);
+    const quire256 v = {{pw[0], pw[1], pw[2], pw[3]}};
+    q = bp::q_add(q, v);
+  }
+  __syncthreads();
+  q = block_reduce_q(q, sh);
+  if (threadIdx.x == 0) {
+    if (q_out) *q_out = q;
+    if (bp16_out) *bp16_out = (uint16_t)bp::from_quire<16>(q, rtne16);
+    if (bp32_out) *bp32_out = bp::from_quire<32>(q, rtne32);
+    *ticket = 0u;  // ready for the next call
+  }
+}
+
+__global__ void fp32_atomic_sum_kernel(const float* __restrict__ x, size_t n, float* acc) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    atomicAdd(acc, x[i]);
+}
+
+template <int NB>
+__global__ void quire_to_bp_kernel(const quire256* __restrict__ q, size_t n, void* out,
+                                   int rtne) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const quire256 v = q[i];
+    const uint32_t r = bp::from_quire<NB>(v, rtne != 0);
+    if (NB == 16)
+      static_cast<uint16_t*>(out)[i] = (uint16_t)r;
+    else
+      static_cast<uint32_t*>(out)[i] = r;
+  }
+}
+
+__global__ void bp16_to_quire_kernel(const uint16_t* __restrict__ x, size_t n,
+                                     quire256* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = bp::quire_from_bp16(x[i]);
+}
+
+__global__ void int32_to_bp32_kernel(const int32_t* __restrict__ in, size_t n, int shift,
+                                     uint32_t* __restrict__ out, int rtne) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = bp::from_int64<32>(in[i], shift, rtne != 0);
+}
+
+template <typename F, int NB>
+__global__ void float_to_bp_kernel(const F* __restrict__ x, size_t n, void* out, int rtne) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t r = bp::from_double<NB>((double)x[i], rtne != 0);
+    if (NB == 16)
+      static_cast<uint16_t*>(out)[i] = (uint16_t)r;
+    else
+      static_cast<uint32_t*>(out)[i] = r;
+  }
+}
+
+unsigned grid_for(size_t n, int num_sms, int per_sm = 8) {
+  size_t b = (n + 255) / 256;
+  const size_t cap = (size_t)num_sms * per_sm;
+  if (b > cap) b = cap;
+  if (b == 0) b = 1;
+  return (unsigned)b;
+}
+
+}  // namespace
+
+int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
+                       uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
+                       int max_blocks) {
+  if (n > 0 && !x) return RC_BAD_ARG;
+  size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
+  size_t cap = (size_t)ctx->num_sms * 4;
+  if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
+    return RC_ALLOC;
+  quire_sum_bp16_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+      x, n, static_cast<quire256*>(ctx->partials), ctx->ticket,
+      reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
+      (flags & MOSYNE_RTNE_BP32) != 0);
+  return launch_rc();
+}
+
+int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
+                        cudaStream_t st) {
+  fp32_atomic_sum_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(x, n, acc);
+  return launch_rc();
+}
+
+int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void* out, int nbits,
+                    int rtne, cudaStream_t st) {
+  if (n == 0) return RC_OK;
+  const auto* qq = reinterpret_cast<const quire256*>(q);
+  if (nbits == 16)
+    quire_to_bp_kernel<16><<<grid_for(n, ctx->num_sms), 256, 0, st>>>(qq, n, out, rtne);
+  else
+    quire_to_bp_kernel<32><<<grid_for(n, ctx->num_sms), 256, 0, st>>>(qq, n, out, rtne);
+  return launch_rc();
+}
+
+int bp16_to_quire_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* out,
+                      cudaStream_t st) {
+  if (n == 0) return RC_OK;
+  bp16_to_quire_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(
+      x, n, reinterpret_cast<quire256*>(out));
+  return launch_rc();
+}
+
+int int32_to_bp32_run(DeviceContext* ctx, const int32_t* in, size_t n, int shift, uint32_t* out,
+                      int rtne, cudaStream_t st) {
+  if (n == 0) return RC_OK;
+  int32_to_bp32_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(in, n, shift, out, rtne);
+  return launch_rc();
+}
+
+int float_to_bposit_run(DeviceContext* ctx, const void* x, int dtype, size_t n, void* out,
+                        int nbits, int rtne, cudaStream_t st) {
+  if (n == 0) return RC_OK;
+  const unsigned g = grid_for(n, ctx->num_sms);
+  if (dtype == MOSYNE_DT_F32) {
+    if (nbits == 16)
+      float_to_bp_kernel<float, 16><<<g, 256, 0, st>>>(static_cast<const float*>(x), n, out, rtne);
+    else
+      float_to_bp_kernel<float, 32><<<g, 256, 0, st>>>(static_cast<const float*>(x), n, out, rtne);
+  } else if (dtype == MOSYNE_DT_F64) {
+    if (nbits == 16)
+      float_to_bp_kernel<double, 16><<<g, 256, 0, st>>>(static_cast<const double*>(x), n, out, rtne);
+    else
+      float_to_bp_kernel<double, 32><<<g, 256, 0, st>>>(static_cast<const double*>(x), n, out, rtne);
+  } else {
+    return RC_BAD_ARG;
+  }
+  return launch_rc();
+}
+
+}  // namespace mb

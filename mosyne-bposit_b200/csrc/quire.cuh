@@ -1,0 +1,21 @@
+// quire.cuh -- exact-sum and conversion entry points used by the C ABI.
+#pragma once
+#include "common.cuh"
+
+namespace mb {
+
+int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
+                       uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
+                       int max_blocks = 0);
+int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
+                        cudaStream_t st);
+int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void* out, int nbits,
+                    int rtne, cudaStream_t st);
+int bp16_to_quire_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* out,
+                      cudaStream_t st);
+int int32_to_bp32_run(DeviceContext* ctx, const int32_t* in, size_t n, int shift, uint32_t* out,
+                      int rtne, cudaStream_t st);
+int float_to_bposit_run(DeviceContext* ctx, const void* x, int dtype, size_t n, void* out,
+                        int nbits, int rtne, cudaStream_t st);
+
+}  // namespace mb

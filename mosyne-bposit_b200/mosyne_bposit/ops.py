@@ -1,0 +1,276 @@
+"""Torch-tensor front end of the C ABI (device tensors in, device tensors out).
+
+Every function allocates its outputs with torch on the input's device and
+launches on the current torch stream; the work itself is the CUDA library's.
+Logical shapes follow the math: a column-major ``[M, N]`` output is returned
+as the ``[M, N]`` transpose view of an ``[N, M]`` allocation.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _api
+
+_DT = {torch.float32: _api.DT_F32, torch.bfloat16: _api.DT_BF16, torch.float16: _api.DT_F16,
+       torch.float64: _api.DT_F64}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("mosyne_bposit ops take CUDA tensors")
+
+
+def _ptr(t):
+    return 0 if t is None else t.data_ptr()
+
+
+def _out(shape_mn, dtype, device, row_major):
+    M, N = shape_mn
+    if row_major:
+        return torch.empty((M, N), dtype=dtype, device=device)
+    return torch.empty((N, M), dtype=dtype, device=device).t()
+
+
+def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool = False,
+            i32: bool = False, y_dtype: torch.dtype | None = None,
+            x_scale: torch.Tensor | None = None, w_scale: torch.Tensor | None = None,
+            rtne32: bool = False, rtne16: bool = False, row_major: bool = False,
+            out: dict | None = None, path: int = 0) -> dict:
+    """Exact ``acc = A @ B^T`` for int8 ``A [M,K]`` and ``B [N,K]`` (both
+    K-contiguous) with the requested encodings of every dot product:
+    ``bp32``/``bp16`` (bposit of the INT32 value), ``i32``, and ``y`` =
+    ``acc / (x_scale[m] * w_scale[n])`` when ``y_dtype`` is given
+    (scalar scales broadcast).  ``out`` may pass preallocated tensors."""
+    _need_cuda(A, B, x_scale, w_scale)
+    if A.dtype != torch.int8 or B.dtype != torch.int8:
+        raise ValueError("A and B must be int8")
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)} vs B {tuple(B.shape)}")
+    A = A.contiguous()
+    B = B.contiguous()
+    M, K = A.shape
+    N = B.shape[0]
+    res = dict(out or {})
+    dev = A.device
+    if bp32 and "bp32" not in res:
+        res["bp32"] = _out((M, N), torch.int32, dev, row_major)
+    if bp16 and "bp16" not in res:
+        res["bp16"] = _out((M, N), torch.int16, dev, row_major)
+    if i32 and "i32" not in res:
+        res["i32"] = _out((M, N), torch.int32, dev, row_major)
+    flags = (_api.RTNE_BP32 if rtne32 else 0) | (_api.RTNE_BP16 if rtne16 else 0) | \
+        (_api.OUT_ROW_MAJOR if row_major else 0)
+    if y_dtype is not None:
+        if x_scale is None or w_scale is None:
+            raise ValueError("dequantised output needs x_scale and w_scale")
+        if x_scale.numel() == 1:
+            flags |= _api.XS_SCALAR
+        if w_scale.numel() == 1:
+            flags |= _api.WS_SCALAR
+        if "y" not in res:
+            res["y"] = _out((M, N), y_dtype, dev, row_major)
+    flags |= (path & 0xF) << 16
+    _api.gemm_i8_dev(A.data_ptr(), B.data_ptr(), M, N, K,
+                     x_scale=_ptr(x_scale), w_scale=_ptr(w_scale),
+                     out_bp32=_ptr(res.get("bp32")), out_bp16=_ptr(res.get("bp16")),
+                     out_y=_ptr(res.get("y")), y_dtype=_DT[y_dtype] if y_dtype else 0,
+                     out_i32=_ptr(res.get("i32")), flags=flags, stream=_stream(A))
+    return res
+
+
+def quantize_per_token(x: torch.Tensor, *, col_major: bool = False):
+    """Per-token int8 quantisation of ``x [M,K]`` -> (``q [M,K]`` K-contiguous,
+    ``scale [M]``).  With ``col_major`` the tensor passed is the ``[K, M]``
+    storage of a column-major ``[M, K]`` matrix (the reference's layout)."""
+    _need_cuda(x)
+    x = x.contiguous()
+    if col_major:
+        K, M = x.shape
+        flags = 0
+    else:
+        M, K = x.shape
+        flags = _api.X_ROW_MAJOR
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    _api.quantize_per_token_dev(x.data_ptr(), _DT[x.dtype], M, K, q.data_ptr(), s.data_ptr(),
+                                flags=flags, stream=_stream(x))
+    return q, s
+
+
+def quantize_per_channel(w: torch.Tensor):
+    """Per-output-channel int8 quantisation of an ``nn.Linear`` weight
+    ``w [N,K]`` (= column-major ``[K,N]``) -> (``q [N,K]``, ``scale [N]``)."""
+    _need_cuda(w)
+    w = w.contiguous()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    s = torch.empty((N,), dtype=torch.float32, device=w.device)
+    _api.quantize_weight_per_channel_ex_dev(w.data_ptr(), _DT[w.dtype], K, N, q.data_ptr(),
+                                            s.data_ptr(), stream=_stream(w))
+    return q, s
+
+
+def quantize_per_tensor(t: torch.Tensor, *, col_major: bool = False):
+    """One-scale int8 quantisation -> (``q`` row-major ``[rows, cols]``,
+    ``scale [1]``).  With ``col_major`` the tensor passed is the ``[cols,
+    rows]`` storage of a column-major matrix and ``q`` is its transpose."""
+    _need_cuda(t)
+    t = t.contiguous()
+    if col_major:
+        cols, rows = t.shape
+        flags = 0
+    else:
+        rows, cols = t.shape
+        flags = _api.X_ROW_MAJOR
+    q = torch.empty((rows, cols), dtype=torch.int8, device=t.device)
+    s = torch.empty((1,), dtype=torch.float32, device=t.device)
+    _api.quantize_per_tensor_dev(t.data_ptr(), _DT[t.dtype], rows, cols, q.data_ptr(),
+                                 s.data_ptr(), flags=flags, stream=_stream(t))
+    return q, s
+
+
+def linear_w8a8(x: torch.Tensor, w_i8: torch.Tensor, w_scale: torch.Tensor, *,
+                out_dtype: torch.dtype | None = None, y: bool = True, bp32: bool = False,
+                bp16: bool = False,
+                per_tensor: bool = False, rtne32: bool = False, rtne16: bool = False) -> dict:
+    """Row-major W8A8 linear: ``x [M,K]`` (fp32/bf16/fp16) and a pre-quantised
+    ``nn.Linear`` weight ``w_i8 [N,K]`` with ``w_scale [N]`` (or ``[1]``).
+    Returns ``{"y": [M,N] in out_dtype (default x.dtype; omitted when
+    ``y=False``), "bp32"?, "bp16"?}``, all row-major, with no transposes.
+    bp32/bp16 encode the raw INT32 dot product (no scales)."""
+    _need_cuda(x, w_i8, w_scale)
+    x = x.contiguous()
+    M, K = x.shape
+    N = w_i8.shape[0]
+    if w_i8.shape[1] != K:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} vs w {tuple(w_i8.shape)}")
+    out_dtype = out_dtype or x.dtype
+    res = {}
+    if y:
+        res["y"] = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    if bp32:
+        res["bp32"] = torch.empty((M, N), dtype=torch.int32, device=x.device)
+    if bp16:
+        res["bp16"] = torch.empty((M, N), dtype=torch.int16, device=x.device)
+    flags = _api.X_ROW_MAJOR | _api.OUT_ROW_MAJOR | (_api.X_PER_TENSOR if per_tensor else 0) | \
+        (_api.WS_SCALAR if w_scale.numel() == 1 and N != 1 else 0) | \
+        (_api.RTNE_BP32 if rtne32 else 0) | (_api.RTNE_BP16 if rtne16 else 0)
+    _api.linear_w8a8_ex_dev(x.data_ptr(), _DT[x.dtype], M, K, w_i8.data_ptr(),
+                            w_scale.data_ptr(), N, y=_ptr(res.get("y")),
+                            y_dtype=_DT[out_dtype] if "y" in res else 0,
+                            y_bp32=_ptr(res.get("bp32")), y_bp16=_ptr(res.get("bp16")),
+                            flags=flags, stream=_stream(x))
+    return res
+
+
+def quire_sum_bp16(x: torch.Tensor, *, rtne16: bool = False, rtne32: bool = False,
+                   max_blocks: int = 0):
+    """Exact sum of bposit16 codes (int16/uint16 tensor) ->
+    (quire words int64 [4], bposit16 code, bposit32 code) as device tensors."""
+    _need_cuda(x)
+    x = x.contiguous()
+    q = torch.empty((4,), dtype=torch.int64, device=x.device)
+    b16 = torch.empty((1,), dtype=torch.int16, device=x.device)
+    b32 = torch.empty((1,), dtype=torch.int32, device=x.device)
+    flags = (_api.RTNE_BP16 if rtne16 else 0) | (_api.RTNE_BP32 if rtne32 else 0) | \
+        ((max_blocks & 0xFFFF) << 16)
+    _api.quire_sum_bp16_dev(x.data_ptr(), x.numel(), q_out=q.data_ptr(), bp16_out=b16.data_ptr(),
+                            bp32_out=b32.data_ptr(), flags=flags, stream=_stream(x))
+    return q, b16, b32
+
+
+def fp32_atomic_sum(x: torch.Tensor) -> torch.Tensor:
+    """The non-deterministic IEEE control: fp32 atomicAdd of every element."""
+    _need_cuda(x)
+    acc = torch.zeros((1,), dtype=torch.float32, device=x.device)
+    _api.fp32_atomic_sum_dev(x.contiguous().data_ptr(), x.numel(), acc.data_ptr(),
+                             stream=_stream(x))
+    return acc
+
+
+def quire_to_bposit(q: torch.Tensor, nbits: int = 16, *, rtne: bool = False) -> torch.Tensor:
+    """``q [n, 4]`` int64 quire words -> bposit16 (int16) or bposit32 (int32)."""
+    _need_cuda(q)
+    q = q.contiguous()
+    n = q.shape[0]
+    out = torch.empty((n,), dtype=torch.int16 if nbits == 16 else torch.int32, device=q.device)
+    _api.quire_to_bposit_dev(q.data_ptr(), n, out.data_ptr(), nbits, rtne=rtne, stream=_stream(q))
+    return out
+
+
+def bp16_to_quire(x: torch.Tensor) -> torch.Tensor:
+    _need_cuda(x)
+    x = x.contiguous()
+    out = torch.empty((x.numel(), 4), dtype=torch.int64, device=x.device)
+    _api.bp16_to_quire_dev(x.data_ptr(), x.numel(), out.data_ptr(), stream=_stream(x))
+    return out
+
+
+def int32_to_bp32(x: torch.Tensor, scale_shift: int = 0, *, rtne: bool = False) -> torch.Tensor:
+    _need_cuda(x)
+    x = x.contiguous()
+    out = torch.empty_like(x, dtype=torch.int32)
+    _api.int32_to_bp32_dev(x.data_ptr(), x.numel(), scale_shift, out.data_ptr(), rtne=rtne,
+                           stream=_stream(x))
+    return out
+
+
+def float_to_bposit(x: torch.Tensor, nbits: int = 16, *, rtne: bool = False) -> torch.Tensor:
+    _need_cuda(x)
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=torch.int16 if nbits == 16 else torch.int32, device=x.device)
+    _api.float_to_bposit_dev(x.data_ptr(), _DT[x.dtype], x.numel(), out.data_ptr(), nbits,
+                             rtne=rtne, stream=_stream(x))
+    return out
+
+
+def epilogue_i32(acc: torch.Tensor, *, bp32: bool = True, bp16: bool = False,
+                 y_dtype: torch.dtype | None = None, x_scale: torch.Tensor | None = None,
+                 w_scale: torch.Tensor | None = None, rtne32: bool = False,
+                 rtne16: bool = False) -> dict:
+    """Epilogue over a logical ``[M,N]`` INT32 accumulator stored column-major
+    (i.e. ``acc`` is the transpose view of an ``[N, M]`` tensor)."""
+    _need_cuda(acc, x_scale, w_scale)
+    M, N = acc.shape
+    store = acc.t()
+    if not store.is_contiguous():
+        store = store.contiguous()
+    res = {}
+    if bp32:
+        res["bp32"] = _out((M, N), torch.int32, acc.device, False)
+    if bp16:
+        res["bp16"] = _out((M, N), torch.int16, acc.device, False)
+    flags = (_api.RTNE_BP32 if rtne32 else 0) | (_api.RTNE_BP16 if rtne16 else 0)
+    if y_dtype is not None:
+        res["y"] = _out((M, N), y_dtype, acc.device, False)
+        if x_scale.numel() == 1:
+            flags |= _api.XS_SCALAR
+        if w_scale.numel() == 1:
+            flags |= _api.WS_SCALAR
+    _api.epilogue_i32_dev(store.data_ptr(), M, N, x_scale=_ptr(x_scale), w_scale=_ptr(w_scale),
+                          out_bp32=_ptr(res.get("bp32")), out_bp16=_ptr(res.get("bp16")),
+                          out_y=_ptr(res.get("y")), y_dtype=_DT[y_dtype] if y_dtype else 0,
+                          flags=flags, stream=_stream(acc))
+    return res
+
+
+def bposit16_op(op: str, a: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """Element-wise bposit16 ALU: add, mul, mul_exact (binary); neg,
+    neg_ones_complement, recip, sqrt, log2, exp2 (unary)."""
+    _need_cuda(a, b)
+    a = a.contiguous()
+    out = torch.empty_like(a, dtype=torch.int16)
+    if b is None:
+        _api.bposit16_unary_dev(op, a.data_ptr(), a.numel(), out.data_ptr(), stream=_stream(a))
+    else:
+        b = b.contiguous()
+        if b.numel() != a.numel():
+            raise ValueError("operands differ in size")
+        _api.bposit16_binary_dev(op, a.data_ptr(), b.data_ptr(), a.numel(), out.data_ptr(),
+                                 stream=_stream(a))
+    return out

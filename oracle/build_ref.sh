@@ -1,0 +1,15 @@
+#!/usr/bin/env bash
+# Build the reference's shipped C-ABI library (one CUDA source file, cuBLASLt
+# from the CUDA toolkit) for sm_100a into oracle/_ref/, as a cross-check of
+# the W8A8 path in the GPU tests.  Test infrastructure only; outputs stay
+# under oracle/_ref/ (git-ignored, carried to the GPU box with the tree).
+set -euo pipefail
+REF=${1:-/root/reference}
+HERE=$(cd "$(dirname "$0")" && pwd)
+SRC="$REF/packages/mosyne_bposit/src/mosyne_bposit/_cuda/libmosyne_bposit.cu"
+[ -f "$SRC" ] || { echo "reference source not found: $SRC" >&2; exit 1; }
+mkdir -p "$HERE/_ref"
+nvcc -O3 -std=c++17 -shared -Xcompiler -fPIC \
+     -gencode arch=compute_100a,code=sm_100a \
+     "$SRC" -o "$HERE/_ref/libmosyne_bposit_ref.so" -lcublasLt -lcudart
+echo "$HERE/_ref/libmosyne_bposit_ref.so"

@@ -1,0 +1,45 @@
+// Host build of the library's encoder header (mosyne-bposit_b200/csrc/bposit.cuh)
+// for CPU tests: the same source the kernels compile, exercised without a GPU.
+#include <cstddef>
+#include <cstdint>
+
+#include "bposit.cuh"
+
+extern "C" {
+
+void h_from_int64(const int64_t* I, const int32_t* shift, size_t n, int nbits, int rtne,
+                  uint32_t* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = nbits == 16 ? bp::from_int64<16>(I[i], shift[i], rtne) : bp::from_int64<32>(I[i], shift[i], rtne);
+}
+
+void h_from_int32(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = nbits == 16 ? bp::from_int32<16>(I[i], rtne) : bp::from_int32<32>(I[i], rtne);
+}
+
+void h_from_quire(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i) {
+    bp::quire256 q{{w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]}};
+    out[i] = nbits == 16 ? bp::from_quire<16>(q, rtne) : bp::from_quire<32>(q, rtne);
+  }
+}
+
+void h_bp16_to_quire(const uint16_t* p, size_t n, uint64_t* w) {
+  for (size_t i = 0; i < n; ++i) {
+    const bp::quire256 q = bp::quire_from_bp16(p[i]);
+    for (int j = 0; j < 4; ++j) w[4 * i + j] = q.w[j];
+  }
+}
+
+void h_from_double(const double* x, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = nbits == 16 ? bp::from_double<16>(x[i], rtne) : bp::from_double<32>(x[i], rtne);
+}
+
+void h_quire_sum(const uint16_t* p, size_t n, uint64_t* w) {
+  bp::quire256 acc = bp::q_zero();
+  for (size_t i = 0; i < n; ++i) acc = bp::q_add(acc, bp::quire_from_bp16(p[i]));
+  for (int j = 0; j < 4; ++j) w[j] = acc.w[j];
+}
+}

@@ -1,0 +1,148 @@
+"""GPU parity: the fused tcgen05 INT8 GEMM vs the oracle.
+
+INT32 accumulators, bposit32/bposit16 codes (truncate and RTNE) and the
+dequantised fp32/bf16/fp16 outputs are compared bit for bit.  Ragged shapes
+cover partial tiles in M, N and K; K not a multiple of 16 takes the CUDA-core
+path.  The full-size check compares the 4096^3 INT32 result with cuBLAS's
+exact integer GEMM and bposit32 codes on a sample against the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import bposit_oracle as O
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+SHAPES = [
+    (128, 256, 128), (1, 1, 16), (7, 9, 32), (129, 257, 144), (300, 520, 1040),
+    (256, 512, 2048), (64, 1000, 4096), (513, 130, 64),
+]
+
+
+def _rand_i8(shape, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randint(-127, 128, shape, generator=g, dtype=torch.int8)
+
+
+def _np(t, dtype=None):
+    a = t.cpu().contiguous().numpy()
+    return a.view(dtype) if dtype is not None else a
+
+
+def _check_all(M, N, K, path=0, row_major=False, seed=0):
+    from mosyne_bposit import ops
+    A = _rand_i8((M, K), seed)
+    B = _rand_i8((N, K), seed + 1)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) * 3 + 0.01
+    ws = torch.rand(N, dtype=torch.float32) * 2 + 0.01
+    Ad, Bd = A.cuda(), B.cuda()
+    for rt in (False, True):
+        r = ops.gemm_i8(Ad, Bd, bp32=True, bp16=True, i32=True, y_dtype=torch.float32,
+                        x_scale=xs.cuda(), w_scale=ws.cuda(), rtne32=rt, rtne16=rt,
+                        row_major=row_major, path=path)
+        torch.cuda.synchronize()
+        mode = "rtne" if rt else "truncate"
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc), (M, N, K, path)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32, mode))
+        assert np.array_equal(_np(r["bp16"], np.uint16), O.encode_int_array(acc, 0, 16, mode))
+        y = O.dequant(acc, xs.numpy(), ws.numpy())
+        assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32))
+    for ydt in (torch.bfloat16, torch.float16):
+        r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=ydt, x_scale=xs.cuda(), w_scale=ws.cuda(),
+                        row_major=row_major, path=path)
+        y = O.dequant(acc, xs.numpy(), ws.numpy())
+        if ydt == torch.bfloat16:
+            assert np.array_equal(_np(r["y"].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y))
+        else:
+            assert np.array_equal(_np(r["y"]).view(np.uint16), y.astype(np.float16).view(np.uint16))
+    from mosyne_bposit import _api
+    assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_tc_auto(cuda_lib, M, N, K):
+    _check_all(M, N, K)
+
+
+@pytest.mark.parametrize("path", [2, 3])   # tile width 128 and 256 forced
+def test_gemm_tc_tile_widths(cuda_lib, path):
+    _check_all(300, 600, 512, path=path)
+    _check_all(1024, 1024, 256, path=path)
+
+
+def test_gemm_row_major_outputs(cuda_lib):
+    _check_all(200, 300, 256, row_major=True)
+
+
+@pytest.mark.parametrize("M,N,K", [(33, 65, 100), (5, 3, 1), (128, 256, 40)])
+def test_gemm_simt_path(cuda_lib, M, N, K):
+    _check_all(M, N, K)          # K % 16 != 0 -> CUDA-core path
+    if K % 16 == 0:
+        _check_all(M, N, K, path=4)
+
+
+def test_gemm_scalar_scales(cuda_lib):
+    from mosyne_bposit import ops
+    M, N, K = 130, 250, 192
+    A, B = _rand_i8((M, K), 5), _rand_i8((N, K), 6)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.tensor([0.37], dtype=torch.float32)
+    ws = torch.tensor([2.5], dtype=torch.float32)
+    r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=False, y_dtype=torch.float32, x_scale=xs.cuda(),
+                    w_scale=ws.cuda())
+    y = O.dequant(acc, np.full(M, 0.37, np.float32), np.full(N, 2.5, np.float32))
+    assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32))
+
+
+def test_gemm_extreme_values(cuda_lib):
+    """All -127 / +127 operands: |acc| = 127^2 K at the top of the int32
+    range used, every output the same sign."""
+    from mosyne_bposit import ops
+    M, N, K = 128, 256, 8192
+    A = torch.full((M, K), -127, dtype=torch.int8)
+    B = torch.full((N, K), 127, dtype=torch.int8)
+    r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=True, i32=True)
+    acc = np.full((M, N), -127 * 127 * K, dtype=np.int64)
+    assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+    assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+
+
+def test_gemm_full_size_4096(cuda_lib):
+    """4096^3 (the headline shape): INT32 equal to cuBLAS's exact integer GEMM;
+    bposit32 codes equal to the oracle's on 2^16 sampled outputs and
+    consistent with encoding the INT32 output everywhere."""
+    from mosyne_bposit import ops
+    M = N = K = 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8, device="cuda")
+    B = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8, device="cuda")
+    r = ops.gemm_i8(A, B, bp32=True, i32=True)
+    ref = torch._int_mm(A, B.t())
+    assert torch.equal(r["i32"], ref)
+    enc = ops.int32_to_bp32(r["i32"].t().contiguous()).t()
+    assert torch.equal(enc, r["bp32"])
+    rng = np.random.default_rng(1)
+    idx = rng.integers(0, M * N, 1 << 16)
+    mi, ni = idx // N, idx % N
+    acc = ref.cpu().numpy().astype(np.int64)[mi, ni]
+    got = r["bp32"].cpu().numpy().view(np.uint32)[mi, ni]
+    assert np.array_equal(got, O.encode_int_array(acc, 0, 32))
+    from mosyne_bposit import _api
+    assert _api.last_error() == 0
+
+
+def test_gemm_bad_args(cuda_lib):
+    from mosyne_bposit import _api
+    lib = cuda_lib
+    assert lib.mosyne_bposit_gemm_i8(0, 0, 4, 4, 16, 0, 0, 0, 0, 0, 0, 0, 0, 0) == -20
+    a = torch.zeros((4, 16), dtype=torch.int8, device="cuda")
+    assert lib.mosyne_bposit_gemm_i8(a.data_ptr(), a.data_ptr(), 0, 4, 16, 0, 0, 0, 0, 0, 0, 0,
+                                     0, 0) == -20
+    # dequant output without scales
+    y = torch.empty((4, 4), device="cuda")
+    assert lib.mosyne_bposit_gemm_i8(a.data_ptr(), a.data_ptr(), 4, 4, 16, 0, 0, 0, 0,
+                                     y.data_ptr(), 0, 0, 0, 0) == -20
+    assert _api.last_error() == 0

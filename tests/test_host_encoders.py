@@ -1,0 +1,104 @@
+"""The library's bposit encoders/decoders (csrc/bposit.cuh, the same source
+the CUDA kernels compile) built for the host with g++ and checked against
+the oracle -- encoder logic verified without a GPU."""
+from __future__ import annotations
+
+import ctypes
+import shutil
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import bposit_oracle as O
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE.parent / "mosyne-bposit_b200" / "csrc"
+
+
+@pytest.fixture(scope="module")
+def hlib(tmp_path_factory):
+    gxx = shutil.which("g++")
+    if not gxx:
+        pytest.skip("g++ not available")
+    out = tmp_path_factory.mktemp("host") / "libhost_encoders.so"
+    subprocess.run([gxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-I", str(CSRC),
+                    str(HERE / "host_encoders.cpp"), "-o", str(out)], check=True)
+    lib = ctypes.CDLL(str(out))
+    return lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def test_int64_encoders(hlib):
+    rng = np.random.default_rng(11)
+    I = np.concatenate([rng.integers(-(2 ** 62), 2 ** 62, 20000), rng.integers(-5000, 5000, 5000),
+                        np.array([0, 1, -1, 2 ** 63 - 1, -(2 ** 63) + 1])]).astype(np.int64)
+    sh = rng.integers(-40, 120, I.size).astype(np.int32)
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(I.size, dtype=np.uint32)
+            hlib.h_from_int64(_p(I), _p(sh), ctypes.c_size_t(I.size), nb, rtne, _p(out))
+            mode = "rtne" if rtne else "truncate"
+            exp = np.array([O.encode_int(int(a), int(s), nb, mode) for a, s in zip(I, sh)], dtype=np.uint32)
+            assert np.array_equal(out, exp), (nb, mode)
+
+
+def test_int32_fast_path(hlib):
+    rng = np.random.default_rng(12)
+    I = np.concatenate([rng.integers(-(2 ** 31), 2 ** 31, 50000), np.arange(-70000, 70000),
+                        np.array([-(2 ** 31), 2 ** 31 - 1])]).astype(np.int32)
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(I.size, dtype=np.uint32)
+            hlib.h_from_int32(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out))
+            exp = O.encode_int_array(I.astype(np.int64), 0, nb, "rtne" if rtne else "truncate")
+            assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
+
+
+def test_quire_encoders(hlib, golden):
+    qs = [int(c["q"]) for c in golden("pyref_samples.json")["quire"]]
+    rng = np.random.default_rng(13)
+    for _ in range(3000):
+        bits = int(rng.integers(0, 250))
+        v = int.from_bytes(rng.bytes(32), "little") & ((1 << bits) - 1)
+        qs.append(v if rng.integers(0, 2) else -v)
+    qs += [_q for _q in (0, 1, -1, (1 << 255) - 1, -(1 << 255) + 1, 1 << 200, -(1 << 200))]
+    w = np.array([O.quire_to_words(q) for q in qs], dtype=np.uint64)
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(len(qs), dtype=np.uint32)
+            hlib.h_from_quire(_p(w), ctypes.c_size_t(len(qs)), nb, rtne, _p(out))
+            mode = "rtne" if rtne else "truncate"
+            exp = np.array([O.quire_to_bposit(q, nb, mode) for q in qs], dtype=np.uint32)
+            assert np.array_equal(out, exp), (nb, mode)
+
+
+def test_bp16_decode_all_codes(hlib):
+    p = np.arange(65536, dtype=np.uint16)
+    w = np.empty((65536, 4), dtype=np.uint64)
+    hlib.h_bp16_to_quire(_p(p), ctypes.c_size_t(65536), _p(w))
+    for i in range(65536):
+        assert O.words_to_quire(w[i]) == O.bposit16_to_quire(i), i
+
+
+def test_double_encoder(hlib):
+    rng = np.random.default_rng(14)
+    x = np.concatenate([rng.standard_normal(20000) * 10.0 ** rng.integers(-20, 20, 20000),
+                        np.array([0.0, -0.0, 5e-324, 1e300, -1e-300, 2.0 ** -48, 2.0 ** 48])])
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(x.size, dtype=np.uint32)
+            hlib.h_from_double(_p(x), ctypes.c_size_t(x.size), nb, rtne, _p(out))
+            exp = O.float_to_bposit_array(x, nb, "rtne" if rtne else "truncate").astype(np.uint32)
+            assert np.array_equal(out, exp), (nb, rtne)
+
+
+def test_headline_sum(hlib, golden):
+    _, _, codes = O.det_headline_inputs()
+    w = np.empty(4, dtype=np.uint64)
+    hlib.h_quire_sum(_p(codes), ctypes.c_size_t(codes.size), _p(w))
+    assert [f"{int(x):016x}" for x in w] == golden("headline.json")["quire_words"]
