@@ -234,20 +234,23 @@ def _cpu_rows_for(M, N, K, target_s, pool):
         rows = min(M, rows * 2 if dt < target_s / 4 else int(rows * target_s / max(dt, 1e-3)) + 1)
 
 
-def cpu_baseline(M, N, K, target_s=8.0):
-    """Timed oracle port on a bounded row block of the workload."""
+def cpu_baseline(M, N, K, target_s=3.0, total_s=10.0):
+    """Timed oracle port on a bounded row block of the workload, repeated
+    for about `total_s` seconds."""
     import numpy as np
     cores = os.cpu_count() or 1
     with cf.ThreadPoolExecutor(cores) as pool:
         rows, dt, B = _cpu_rows_for(M, N, K, target_s, pool)
         A = np.random.default_rng(1).integers(-127, 128, (rows, K), dtype=np.int8)
+        reps = max(1, int(total_s / max(dt, 1e-3)))
         t0 = time.perf_counter()
-        _cpu_port_step(A, B, pool)
-        dt = time.perf_counter() - t0
+        for _ in range(reps):
+            _cpu_port_step(A, B, pool)
+        dt = (time.perf_counter() - t0) / reps
     return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{rows} of {M} rows of the {M}x{N}x{K} GEMM (all {N} columns, full K), "
                       f"numpy float64-BLAS exact GEMM + vectorised bposit32 encode of every "
-                      f"output on {cores} threads; {dt:.2f} s"}
+                      f"output on {cores} threads; {reps} repetitions, {dt:.2f} s each"}
 
 
 def run_reference(args):
@@ -356,16 +359,35 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_only_gemm(args):
+    import torch
+
+    from mosyne_bposit import _api
+    torch.cuda.set_device(0)
+    lib = _api.load_library(init=True)
+    M, N, K = (int(v) for v in args.only_gemm.split(","))
+    ms, nsets, _ = _time_gemm(M, N, K, args.steps, args.warmup, None, 1,
+                              lambda A, B, out, st: _ours(A, B, out, st, lib))
+    rc = _api.last_error()
+    per = ms / args.steps
+    print(json.dumps({"shape": [M, N, K], "ms_per_launch": per, "tpops": 2.0 * M * N * K / per / 1e9,
+                      "buffer_sets": nsets, "device_error": rc}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--only-gemm", default=None, metavar="M,N,K",
+                    help="time only the fused GEMM at this shape (for profilers); prints one line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only_gemm:
+        run_only_gemm(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -161,6 +161,19 @@ int mosyne_bposit_quantize_per_tensor(const void* t, int dtype, int rows, int co
                                       int8_t* q, float* scale, int flags,
                                       mosyne_stream_t stream);
 
+/* Per-row |max| of x [M,K] (column-major, or row-major with
+ * MOSYNE_X_ROW_MAJOR) into row_max[M] -- the first half of the per-token
+ * quantiser (libmosyne_bposit.cu:215-233), exposed so a K-split across GPUs
+ * can reduce the maxima before quantising (max is exact and order free). */
+int mosyne_bposit_row_absmax(const void* x, int x_dtype, int M, int K, float* row_max, int flags,
+                             mosyne_stream_t stream);
+
+/* The second half (libmosyne_bposit.cu:234-243) with caller-supplied row
+ * maxima: x_scale[m] = 127/row_max[m], x_i8 [M,K] K contiguous. */
+int mosyne_bposit_quantize_with_max(const void* x, int x_dtype, int M, int K, const float* row_max,
+                                    int8_t* x_i8, float* x_scale, int flags,
+                                    mosyne_stream_t stream);
+
 /* libmosyne_bposit.cu:162-193 on a stream, for fp32/bf16/fp16 weights. */
 int mosyne_bposit_quantize_weight_per_channel_ex(const void* w, int dtype, int K, int N,
                                                  int8_t* w_i8_out, float* w_scale_out,

@@ -94,15 +94,73 @@ BP_HD uint32_t from_int64(int64_t I, int shift, bool rtne) {
 
 // Fast path for an INT32 accumulator (value = I, no fraction bits):
 // int_to_bposit32(I, 0) of kernels/test_int32_to_bposit32.cu:94-112, equal
-// to quire256_to_bposit32(I << 96).  scale = msb in [0, 31] never saturates.
+// to quire256_to_bposit32(I << 96).  scale = msb in [0, 31], so the regime is
+// always k+1 ones (k <= 3) and nothing saturates: straight-line code with no
+// branches, which lets the GEMM epilogue interleave many outputs.
 template <int NBITS>
 BP_HD uint32_t from_int32(int32_t I, bool rtne) {
-  if (I == 0) return 0u;
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
   const bool neg = I < 0;
   const uint32_t a = neg ? 0u - (uint32_t)I : (uint32_t)I;
+  const int lz = clz32(a | 1u);                         // a == 0 is selected away below
+  const int msb = 31 - lz;
+  const int k = msb >> 3, e = msb & 7;
+  const uint32_t regime = ((2u << k) - 1u) << (N1 - 1 - k);
+  const int fw = N1 - 5 - k;                            // N1 - (k + 2) - 3
+  const uint32_t frac = (a << lz) << 1;                 // MSB-aligned fraction bits
+  uint32_t field = regime | ((uint32_t)e << fw) | (frac >> (32 - fw));
+  const uint32_t rest = frac << fw;
+  const uint32_t up = (uint32_t)rtne & (rest >> 31) & (uint32_t)(((rest << 1) != 0u) | (field & 1u)) &
+                      (uint32_t)(field < FMASK);
+  field += up;
+  const uint32_t out = neg ? ((1u << N1) | ((0u - field) & FMASK)) : field;
+  return a == 0u ? 0u : out;
+}
+
+// Table-driven INT32 -> bposit for the GEMM epilogue.  For lz = clz(|I|)
+// the regime, exponent and fraction width depend only on lz, so a 33-entry
+// table (lz = 0..32, 32 meaning I == 0) holds
+//   prefix = (regime | e << fw) ^ 1 << fw   and   sh = 31 - fw;
+// with x = |I| << lz (leading one at bit 31), x >> sh puts the leading one at
+// bit fw and the kept fraction below it, and prefix ^ (x >> sh) clears the
+// leading one: the magnitude field in ~10 integer operations.  Equal to
+// from_int32 for every input (checked exhaustively over the scale range in
+// the host tests).
+struct I32Entry {
+  uint32_t prefix;
+  uint32_t sh;
+};
+
+template <int NBITS>
+BP_HD I32Entry i32_table_entry(int lz) {
+  constexpr int N1 = NBITS - 1;
+  if (lz >= 32) return I32Entry{0u, 31u};
+  const int msb = 31 - lz;
+  const int k = msb >> 3, e = msb & 7;
+  const int fw = N1 - 5 - k;
+  const uint32_t regime = ((2u << k) - 1u) << (N1 - 1 - k);
+  return I32Entry{(regime | ((uint32_t)e << fw)) ^ (1u << fw), (uint32_t)(31 - fw)};
+}
+
+template <int NBITS, bool RTNE>
+BP_HD uint32_t from_int32_tab(int32_t I, const I32Entry* tab) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  const uint32_t m = (uint32_t)(I >> 31);                // all ones when negative
+  const uint32_t a = ((uint32_t)I ^ m) - m;
   const int lz = clz32(a);
-  const uint64_t frac = (uint64_t)((a << lz) << 1) << 32;
-  return apply_sign<NBITS>(encode_field<NBITS>(31 - lz, frac, false, rtne), neg);
+  const I32Entry t = tab[lz];
+  const uint32_t x = a << (lz & 31);
+  uint32_t field = t.prefix ^ (x >> t.sh);
+  if (RTNE) {
+    const uint32_t rem = x << (32 - t.sh);                // round bit at 31, sticky below
+    const uint32_t up = (rem >> 31) & (uint32_t)(((rem << 1) != 0u) | (field & 1u)) &
+                        (uint32_t)(field != FMASK);
+    field += up;
+  }
+  const uint32_t out = (field ^ m) - m;
+  return NBITS == 32 ? out : (out & 0xFFFFu);
 }
 
 // ---------------------------------------------------------------------------

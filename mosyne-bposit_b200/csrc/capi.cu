@@ -350,6 +350,25 @@ int mosyne_bposit_quantize_per_tensor(const void* t, int dtype, int rows, int co
                           true, as_stream(stream));
 }
 
+int mosyne_bposit_row_absmax(const void* x, int x_dtype, int M, int K, float* row_max, int flags,
+                             mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || K <= 0 || !x || !row_max || !dtype_ok(x_dtype)) return RC_BAD_ARG;
+  return row_absmax(ctx, x_dtype, x, M, K, row_max, (flags & MOSYNE_X_ROW_MAJOR) != 0,
+                    as_stream(stream));
+}
+
+int mosyne_bposit_quantize_with_max(const void* x, int x_dtype, int M, int K, const float* row_max,
+                                    int8_t* x_i8, float* x_scale, int flags,
+                                    mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || K <= 0 || !x || !row_max || !x_i8 || !dtype_ok(x_dtype)) return RC_BAD_ARG;
+  return quant_with_max(x_dtype, x, M, K, row_max, x_i8, x_scale,
+                        (flags & MOSYNE_X_ROW_MAJOR) != 0, as_stream(stream));
+}
+
 int mosyne_bposit_quantize_weight_per_channel_ex(const void* w, int dtype, int K, int N,
                                                  int8_t* w_i8_out, float* w_scale_out,
                                                  mosyne_stream_t stream) {

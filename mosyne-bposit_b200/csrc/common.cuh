@@ -6,7 +6,7 @@
 #include <cstddef>
 #include <cstdint>
 
-#include "../../include/mosyne_bposit.h"
+#include "mosyne_bposit.h"
 
 namespace mb {
 

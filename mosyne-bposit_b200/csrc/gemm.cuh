@@ -30,6 +30,7 @@ enum GemmPath {
   GEMM_PATH_TC_BN128 = 2,
   GEMM_PATH_TC_BN256 = 3,
   GEMM_PATH_SIMT = 4,
+  GEMM_PATH_TC_PAIR = 5,   // CTA-pair (cta_group::2) 256x256 tiles
 };
 
 // acc = A[M,K] (K contiguous) x B[N,K]^T (K contiguous), fused epilogue.

@@ -40,7 +40,8 @@ template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x, int R, int C,
                                                          int8_t* __restrict__ q,
                                                          float* __restrict__ scale,
-                                                         const uint32_t* __restrict__ given_amax) {
+                                                         const uint32_t* __restrict__ given_amax,
+                                                         int amax_stride) {
   constexpr int V = Vec<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   int8_t* qr = q + (size_t)row * C;
   float m = 0.f;
   if (given_amax) {
-    m = __uint_as_float(*given_amax);
+    m = __uint_as_float(given_amax[(size_t)row * amax_stride]);
   } else {
     if (VEC) {
       for (int c = lane * V; c < C; c += 32 * V) {
@@ -184,16 +185,32 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
+// Row-major [R, C]: |max| of each row into amax[R] (fp32 bit patterns).
+template <typename T>
+__global__ void __launch_bounds__(256) rowmax_rows_kernel(const T* __restrict__ x, int R, int C,
+                                                          uint32_t* __restrict__ amax) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= R) return;
+  const T* xr = x + (size_t)row * C;
+  float m = 0.f;
+  for (int c = lane; c < C; c += 32) m = fmaxf(m, fabsf(to_f32<T>(xr[c])));
+  m = warp_max(m);
+  if (lane == 0) amax[row] = __float_as_uint(m);
+}
+
 template <typename T>
 int quant_rows_t(const void* x, int R, int C, int8_t* q, float* scale, const uint32_t* amax,
-                 cudaStream_t st) {
+                 cudaStream_t st, int amax_stride = 0) {
   constexpr int V = Vec<T>::N;
   const bool vec = (C % V == 0) && aligned16<T>(x) && ((reinterpret_cast<uintptr_t>(q) % V) == 0);
   const unsigned blocks = (unsigned)((R + 7) / 8);
   if (vec)
-    quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax);
+    quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
+                                                       amax_stride);
   else
-    quant_rows_kernel<T, false><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax);
+    quant_rows_kernel<T, false><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
+                                                        amax_stride);
   return launch_rc();
 }
 
@@ -260,6 +277,56 @@ int quant_rows(int dtype, const void* x, int R, int C, int8_t* q, float* scale, 
     case MOSYNE_DT_F32: return quant_rows_t<float>(x, R, C, q, scale, nullptr, st);
     case MOSYNE_DT_BF16: return quant_rows_t<__nv_bfloat16>(x, R, C, q, scale, nullptr, st);
     case MOSYNE_DT_F16: return quant_rows_t<__half>(x, R, C, q, scale, nullptr, st);
+    default: return RC_BAD_ARG;
+  }
+}
+
+int row_absmax(DeviceContext* ctx, int dtype, const void* x, int M, int K, float* out,
+               bool row_major, cudaStream_t st) {
+  if (M <= 0 || K <= 0) return RC_BAD_ARG;
+  uint32_t* o = reinterpret_cast<uint32_t*>(out);
+  if (row_major) {
+    const unsigned blocks = (unsigned)((M + 7) / 8);
+    switch (dtype) {
+      case MOSYNE_DT_F32: rowmax_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), M, K, o); break;
+      case MOSYNE_DT_BF16: rowmax_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, o); break;
+      case MOSYNE_DT_F16: rowmax_rows_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), M, K, o); break;
+      default: return RC_BAD_ARG;
+    }
+    return launch_rc();
+  }
+  cudaMemsetAsync(o, 0, (size_t)M * sizeof(uint32_t), st);
+  const int gm = (M + 63) / 64;
+  int splits = (2 * ctx->num_sms + gm - 1) / gm;
+  splits = max(1, min(splits, (K + 63) / 64));
+  const int k_chunk = (K + splits - 1) / splits;
+  const dim3 grid(gm, (K + k_chunk - 1) / k_chunk);
+  switch (dtype) {
+    case MOSYNE_DT_F32: colmajor_rowmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), M, K, k_chunk, o); break;
+    case MOSYNE_DT_BF16: colmajor_rowmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, k_chunk, o); break;
+    case MOSYNE_DT_F16: colmajor_rowmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), M, K, k_chunk, o); break;
+    default: return RC_BAD_ARG;
+  }
+  return launch_rc();
+}
+
+template <typename T>
+int quant_given_t(const void* x, int M, int K, const float* row_max, int8_t* q, float* scale,
+                  bool row_major, cudaStream_t st) {
+  const uint32_t* am = reinterpret_cast<const uint32_t*>(row_max);
+  if (row_major) return quant_rows_t<T>(x, M, K, q, scale, am, st, 1);
+  colmajor_quant_kernel<T><<<dim3((M + 63) / 64, (K + 63) / 64), 256, 0, st>>>(
+      static_cast<const T*>(x), M, K, am, 1, q, scale);
+  return launch_rc();
+}
+
+int quant_with_max(int dtype, const void* x, int M, int K, const float* row_max, int8_t* q,
+                   float* scale, bool row_major, cudaStream_t st) {
+  if (M <= 0 || K <= 0) return RC_BAD_ARG;
+  switch (dtype) {
+    case MOSYNE_DT_F32: return quant_given_t<float>(x, M, K, row_max, q, scale, row_major, st);
+    case MOSYNE_DT_BF16: return quant_given_t<__nv_bfloat16>(x, M, K, row_max, q, scale, row_major, st);
+    case MOSYNE_DT_F16: return quant_given_t<__half>(x, M, K, row_max, q, scale, row_major, st);
     default: return RC_BAD_ARG;
   }
 }

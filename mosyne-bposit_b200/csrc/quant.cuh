@@ -13,6 +13,15 @@ int quant_rows(int dtype, const void* x, int R, int C, int8_t* q, float* scale, 
 int quant_activation(DeviceContext* ctx, int dtype, const void* x, int M, int K, int8_t* q,
                      float* scale, bool row_major, bool per_tensor, cudaStream_t st);
 
+// |max| of every row of x [M,K] (row-major or column-major) -> out[M] (fp32).
+int row_absmax(DeviceContext* ctx, int dtype, const void* x, int M, int K, float* out,
+               bool row_major, cudaStream_t st);
+
+// Per-row quantisation with caller-supplied row maxima (e.g. reduced across
+// GPUs): scale[m] = 127 / row_max[m]; q row-major [M,K].
+int quant_with_max(int dtype, const void* x, int M, int K, const float* row_max, int8_t* q,
+                   float* scale, bool row_major, cudaStream_t st);
+
 int write_scalar_scale(const uint32_t* amax, float* scale, cudaStream_t st);
 
 }  // namespace mb

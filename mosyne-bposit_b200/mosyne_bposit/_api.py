@@ -70,6 +70,8 @@ _SIGS = {
     "mosyne_bposit_quantize_per_token": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "mosyne_bposit_quantize_per_tensor": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "mosyne_bposit_quantize_weight_per_channel_ex": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "mosyne_bposit_row_absmax": (_I, [_P, _I, _I, _I, _P, _I, _P]),
+    "mosyne_bposit_quantize_with_max": (_I, [_P, _I, _I, _I, _P, _P, _P, _I, _P]),
     "mosyne_bposit_quire_sum_bp16": (_I, [_P, _SZ, _P, _P, _P, _I, _P]),
     "mosyne_bposit_fp32_atomic_sum": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit_quire_to_bp16": (_I, [_P, _SZ, _P, _I, _P]),
@@ -284,6 +286,20 @@ def quantize_weight_per_channel_ex_dev(w: int, dtype: int, K: int, N: int, w_i8:
     lib = _ensure_library()
     _check(lib.mosyne_bposit_quantize_weight_per_channel_ex(w, dtype, K, N, w_i8, w_scale, stream),
            "mosyne_bposit_quantize_weight_per_channel_ex")
+
+
+def row_absmax_dev(x: int, x_dtype: int, M: int, K: int, row_max: int, *, flags: int = 0,
+                   stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_row_absmax(x, x_dtype, M, K, row_max, flags, stream),
+           "mosyne_bposit_row_absmax")
+
+
+def quantize_with_max_dev(x: int, x_dtype: int, M: int, K: int, row_max: int, x_i8: int,
+                          x_scale: int, *, flags: int = 0, stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_quantize_with_max(x, x_dtype, M, K, row_max, x_i8, x_scale, flags,
+                                               stream), "mosyne_bposit_quantize_with_max")
 
 
 def quire_sum_bp16_dev(x: int, n: int, *, q_out: int = 0, bp16_out: int = 0, bp32_out: int = 0,

@@ -134,6 +134,30 @@ def quantize_per_tensor(t: torch.Tensor, *, col_major: bool = False):
     return q, s
 
 
+def row_absmax(x: torch.Tensor) -> torch.Tensor:
+    """|max| of every row of a row-major ``x [M,K]`` (fp32 ``[M]``)."""
+    _need_cuda(x)
+    x = x.contiguous()
+    M, K = x.shape
+    out = torch.empty((M,), dtype=torch.float32, device=x.device)
+    _api.row_absmax_dev(x.data_ptr(), _DT[x.dtype], M, K, out.data_ptr(), flags=_api.X_ROW_MAJOR,
+                        stream=_stream(x))
+    return out
+
+
+def quantize_with_max(x: torch.Tensor, row_max: torch.Tensor):
+    """Per-token quantisation of row-major ``x [M,K]`` with given row maxima
+    -> (``q [M,K]``, ``scale [M]``)."""
+    _need_cuda(x, row_max)
+    x = x.contiguous()
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    _api.quantize_with_max_dev(x.data_ptr(), _DT[x.dtype], M, K, row_max.contiguous().data_ptr(),
+                               q.data_ptr(), s.data_ptr(), flags=_api.X_ROW_MAJOR, stream=_stream(x))
+    return q, s
+
+
 def linear_w8a8(x: torch.Tensor, w_i8: torch.Tensor, w_scale: torch.Tensor, *,
                 out_dtype: torch.dtype | None = None, y: bool = True, bp32: bool = False,
                 bp16: bool = False,

@@ -18,6 +18,20 @@ void h_from_int32(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out
     out[i] = nbits == 16 ? bp::from_int32<16>(I[i], rtne) : bp::from_int32<32>(I[i], rtne);
 }
 
+void h_from_int32_tab(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out) {
+  bp::I32Entry t16[33], t32[33];
+  for (int i = 0; i < 33; ++i) {
+    t16[i] = bp::i32_table_entry<16>(i);
+    t32[i] = bp::i32_table_entry<32>(i);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    if (nbits == 16)
+      out[i] = rtne ? bp::from_int32_tab<16, true>(I[i], t16) : bp::from_int32_tab<16, false>(I[i], t16);
+    else
+      out[i] = rtne ? bp::from_int32_tab<32, true>(I[i], t32) : bp::from_int32_tab<32, false>(I[i], t32);
+  }
+}
+
 void h_from_quire(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* out) {
   for (size_t i = 0; i < n; ++i) {
     bp::quire256 q{{w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]}};

@@ -67,10 +67,12 @@ def test_gemm_tc_auto(cuda_lib, M, N, K):
     _check_all(M, N, K)
 
 
-@pytest.mark.parametrize("path", [2, 3])   # tile width 128 and 256 forced
+@pytest.mark.parametrize("path", [2, 3, 5])   # one-CTA tile width 128 / 256, CTA pair
 def test_gemm_tc_tile_widths(cuda_lib, path):
     _check_all(300, 600, 512, path=path)
     _check_all(1024, 1024, 256, path=path)
+    _check_all(64, 200, 160, path=path)
+    _check_all(777, 257, 2064, path=path, row_major=True)
 
 
 def test_gemm_row_major_outputs(cuda_lib):

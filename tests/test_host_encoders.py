@@ -59,6 +59,26 @@ def test_int32_fast_path(hlib):
             assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
 
 
+def test_int32_table_path(hlib):
+    """The epilogue's table-driven encoder equals the oracle on every scale
+    (each power of two and its neighbours) and on random values."""
+    rng = np.random.default_rng(15)
+    edges = []
+    for b in range(31):
+        for d in (-2, -1, 0, 1, 2):
+            v = (1 << b) + d
+            if 0 < v < 2 ** 31:
+                edges += [v, -v]
+    I = np.concatenate([rng.integers(-(2 ** 31), 2 ** 31, 200000), np.array(edges),
+                        np.array([0, -(2 ** 31), 2 ** 31 - 1])]).astype(np.int32)
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(I.size, dtype=np.uint32)
+            hlib.h_from_int32_tab(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out))
+            exp = O.encode_int_array(I.astype(np.int64), 0, nb, "rtne" if rtne else "truncate")
+            assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
+
+
 def test_quire_encoders(hlib, golden):
     qs = [int(c["q"]) for c in golden("pyref_samples.json")["quire"]]
     rng = np.random.default_rng(13)
