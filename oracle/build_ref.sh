@@ -7,7 +7,7 @@ set -euo pipefail
 REF=${1:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
 SRC="$REF/packages/mosyne_bposit/src/mosyne_bposit/_cuda/libmosyne_bposit.cu"
-[ -f "$SRC" ] || { echo "reference source not found: $SRC" >&2; exit 1; }
+if [ ! -f "$SRC" ]; then echo "reference sources not present; nothing to build"; exit 0; fi
 mkdir -p "$HERE/_ref"
 nvcc -O3 -std=c++17 -shared -Xcompiler -fPIC \
      -gencode arch=compute_100a,code=sm_100a \
