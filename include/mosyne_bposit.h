@@ -239,6 +239,26 @@ int mosyne_bposit16_sqrt(const uint16_t* a, size_t n, uint16_t* out, mosyne_stre
 int mosyne_bposit16_log2(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
 int mosyne_bposit16_exp2(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream);
 
+/* Return code: the input does not fit the fixed scratch of
+ * mosyne_bposit_linear_w8a8_noalloc. */
+#define MOSYNE_RC_SCRATCH_LIMIT (-21)
+
+/* No counterpart in the reference: mosyne_bposit_linear_w8a8 that allocates
+ * no device memory, for callers that cannot call cudaMalloc (a serving
+ * process whose device memory belongs to a caching allocator or is capped, a
+ * plugin host that forbids raw allocations, code that must avoid the device
+ * synchronisation an allocation can cause).  Same arguments, layouts and
+ * results as mosyne_bposit_linear_w8a8, plus a stream; needs no
+ * mosyne_bposit_init.  Its scratch is one fixed static device array (about
+ * 8.1 MiB, held by every GPU that loads the library until exit): M <= 16384
+ * and M*K <= 8 MiB, else -21.  The first call on each device looks that array
+ * up (cudaGetSymbolAddress) and should come before any stream capture.  All
+ * calls share the array: calls that may overlap on the GPU race, so order
+ * them on one stream. */
+int mosyne_bposit_linear_w8a8_noalloc(const float* d_x_fp32, int M, int K, const int8_t* d_w_i8,
+                                      const float* d_w_scale, int N, float* d_y_fp32,
+                                      mosyne_stream_t stream);
+
 /* Copies one of the device-resident ALU tables (0 log2, 1 exp2, 2 sqrt,
  * 3 recip; 65,536 u16) to host memory, for verification. */
 int mosyne_bposit16_table_host(int which, uint16_t* host_out);

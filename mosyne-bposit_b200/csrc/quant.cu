@@ -331,6 +331,32 @@ int quant_with_max(int dtype, const void* x, int M, int K, const float* row_max,
   }
 }
 
+template <typename T>
+int colmajor_per_token_into_t(const void* x, int M, int K, int8_t* q, float* scale, uint32_t* amax,
+                              int num_sms, cudaStream_t st) {
+  if (cudaMemsetAsync(amax, 0, (size_t)M * sizeof(uint32_t), st) != cudaSuccess) return RC_LAUNCH;
+  const int gm = (M + 63) / 64;
+  int splits = (2 * num_sms + gm - 1) / gm;
+  splits = max(1, min(splits, (K + 63) / 64));
+  const int k_chunk = (K + splits - 1) / splits;
+  colmajor_rowmax_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
+      static_cast<const T*>(x), M, K, k_chunk, amax);
+  colmajor_quant_kernel<T><<<dim3(gm, (K + 63) / 64), 256, 0, st>>>(static_cast<const T*>(x), M, K,
+                                                                    amax, 1, q, scale);
+  return launch_rc();
+}
+
+int quant_per_token_colmajor_into(int dtype, const void* x, int M, int K, int8_t* q, float* scale,
+                                  uint32_t* amax_scratch, int num_sms, cudaStream_t st) {
+  if (M <= 0 || K <= 0) return RC_BAD_ARG;
+  switch (dtype) {
+    case MOSYNE_DT_F32: return colmajor_per_token_into_t<float>(x, M, K, q, scale, amax_scratch, num_sms, st);
+    case MOSYNE_DT_BF16: return colmajor_per_token_into_t<__nv_bfloat16>(x, M, K, q, scale, amax_scratch, num_sms, st);
+    case MOSYNE_DT_F16: return colmajor_per_token_into_t<__half>(x, M, K, q, scale, amax_scratch, num_sms, st);
+    default: return RC_BAD_ARG;
+  }
+}
+
 int quant_activation(DeviceContext* ctx, int dtype, const void* x, int M, int K, int8_t* q,
                      float* scale, bool row_major, bool per_tensor, cudaStream_t st) {
   if (M <= 0 || K <= 0) return RC_BAD_ARG;

@@ -22,6 +22,11 @@ int row_absmax(DeviceContext* ctx, int dtype, const void* x, int M, int K, float
 int quant_with_max(int dtype, const void* x, int M, int K, const float* row_max, int8_t* q,
                    float* scale, bool row_major, cudaStream_t st);
 
+// Column-major per-token quantisation into caller-provided buffers, the row
+// maxima included (no library scratch).
+int quant_per_token_colmajor_into(int dtype, const void* x, int M, int K, int8_t* q, float* scale,
+                                  uint32_t* amax_scratch, int num_sms, cudaStream_t st);
+
 int write_scalar_scale(const uint32_t* amax, float* scale, cudaStream_t st);
 
 }  // namespace mb
