@@ -168,11 +168,11 @@ def _time_gemm(M, N, K, steps, warmup, dist, seed, lib_call):
     return ms, nsets, out
 
 
-def _ours(A, B, out, stream, lib):
+def _ours(A, B, out, stream, lib, flags=0):
     M, K = A.shape
     N = B.shape[0]
     rc = lib.mosyne_bposit_gemm_i8(A.data_ptr(), B.data_ptr(), M, N, K, 0, 0, out.data_ptr(), 0, 0,
-                                   0, 0, 0, stream.cuda_stream)
+                                   0, 0, flags, stream.cuda_stream)
     if rc != 0:
         raise RuntimeError(f"mosyne_bposit_gemm_i8 rc={rc}")
 
@@ -367,11 +367,12 @@ def run_only_gemm(args):
     lib = _api.load_library(init=True)
     M, N, K = (int(v) for v in args.only_gemm.split(","))
     ms, nsets, _ = _time_gemm(M, N, K, args.steps, args.warmup, None, 1,
-                              lambda A, B, out, st: _ours(A, B, out, st, lib))
+                              lambda A, B, out, st: _ours(A, B, out, st, lib, args.gemm_flags))
     rc = _api.last_error()
     per = ms / args.steps
-    print(json.dumps({"shape": [M, N, K], "ms_per_launch": per, "tpops": 2.0 * M * N * K / per / 1e9,
-                      "buffer_sets": nsets, "device_error": rc}), flush=True)
+    print(json.dumps({"shape": [M, N, K], "flags": args.gemm_flags, "ms_per_launch": per,
+                      "tpops": 2.0 * M * N * K / per / 1e9, "buffer_sets": nsets,
+                      "device_error": rc}), flush=True)
 
 
 def main():
@@ -382,6 +383,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--only-gemm", default=None, metavar="M,N,K",
                     help="time only the fused GEMM at this shape (for profilers); prints one line")
+    ap.add_argument("--gemm-flags", type=lambda v: int(v, 0), default=0,
+                    help="flags word passed to mosyne_bposit_gemm_i8 with --only-gemm "
+                         "(e.g. 0x100000 * (1 + cut) pins the last-wave cut)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -163,6 +163,35 @@ BP_HD uint32_t from_int32_tab(int32_t I, const I32Entry* tab) {
   return NBITS == 32 ? out : (out & 0xFFFFu);
 }
 
+// The same encoding with the table entry computed in registers: no memory
+// access per value.  The magnitude's leading one sits at bit msb = 31 - lz, so
+// the regime run is k + 1 = (msb >> 3) + 1 ones and the fraction field is
+// fw = NBITS - 6 - k bits wide; x >> sh puts the hidden one at bit fw, where
+// the XOR with (e ^ 1) << fw turns it back into the exponent's low bit.
+template <int NBITS, bool RTNE>
+BP_HD uint32_t from_int32_alu(int32_t I) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  const uint32_t m = (uint32_t)(I >> 31);                // all ones when negative
+  const uint32_t a = ((uint32_t)I ^ m) - m;
+  const int lz = clz32(a);
+  const int msb = 31 - lz;
+  const int k = (msb >> 3) & 3;
+  const int fw = NBITS - 6 - k;
+  const int sh = 37 - NBITS + k;
+  const uint32_t regime = (1u << N1) - ((1u << (N1 - 1)) >> k);
+  const uint32_t x = a << (lz & 31);
+  uint32_t field = (regime | ((uint32_t)((msb & 7) ^ 1) << fw)) ^ (x >> sh);
+  if (RTNE) {
+    const uint32_t rem = x << (32 - sh);                   // round bit at 31, sticky below
+    const uint32_t up = (rem >> 31) & (uint32_t)(((rem << 1) != 0u) | (field & 1u)) &
+                        (uint32_t)(field != FMASK);
+    field += up;
+  }
+  const uint32_t out = a ? (field ^ m) - m : 0u;
+  return NBITS == 32 ? out : (out & 0xFFFFu);
+}
+
 // ---------------------------------------------------------------------------
 // quire256
 // ---------------------------------------------------------------------------

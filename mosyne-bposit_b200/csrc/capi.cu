@@ -293,7 +293,7 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
   p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
   p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
   p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
-  const int path = (flags >> 16) & 0xF;  // test hook: force a GEMM path
+  const int path = (flags >> 16) & 0x3F;  // test hook: force a GEMM path / tail cut
   return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
 }
 

@@ -40,12 +40,15 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
             i32: bool = False, y_dtype: torch.dtype | None = None,
             x_scale: torch.Tensor | None = None, w_scale: torch.Tensor | None = None,
             rtne32: bool = False, rtne16: bool = False, row_major: bool = False,
-            out: dict | None = None, path: int = 0) -> dict:
+            out: dict | None = None, path: int = 0, tail: int = 0) -> dict:
     """Exact ``acc = A @ B^T`` for int8 ``A [M,K]`` and ``B [N,K]`` (both
     K-contiguous) with the requested encodings of every dot product:
     ``bp32``/``bp16`` (bposit of the INT32 value), ``i32``, and ``y`` =
     ``acc / (x_scale[m] * w_scale[n])`` when ``y_dtype`` is given
-    (scalar scales broadcast).  ``out`` may pass preallocated tensors."""
+    (scalar scales broadcast).  ``out`` may pass preallocated tensors.
+    ``path`` and ``tail`` pin the kernel choice (tests): path 1 tensor cores,
+    2/3 one-CTA tiles 128/256 wide, 4 CUDA cores, 5 CTA pairs; tail 1/2/3 cuts
+    the CTA-pair kernel's last wave into whole/half/quarter tiles."""
     _need_cuda(A, B, x_scale, w_scale)
     if A.dtype != torch.int8 or B.dtype != torch.int8:
         raise ValueError("A and B must be int8")
@@ -74,7 +77,7 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
             flags |= _api.WS_SCALAR
         if "y" not in res:
             res["y"] = _out((M, N), y_dtype, dev, row_major)
-    flags |= (path & 0xF) << 16
+    flags |= ((path & 0xF) << 16) | ((tail & 0x3) << 20)
     _api.gemm_i8_dev(A.data_ptr(), B.data_ptr(), M, N, K,
                      x_scale=_ptr(x_scale), w_scale=_ptr(w_scale),
                      out_bp32=_ptr(res.get("bp32")), out_bp16=_ptr(res.get("bp16")),

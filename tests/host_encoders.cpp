@@ -32,6 +32,15 @@ void h_from_int32_tab(const int32_t* I, size_t n, int nbits, int rtne, uint32_t*
   }
 }
 
+void h_from_int32_alu(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i) {
+    if (nbits == 16)
+      out[i] = rtne ? bp::from_int32_alu<16, true>(I[i]) : bp::from_int32_alu<16, false>(I[i]);
+    else
+      out[i] = rtne ? bp::from_int32_alu<32, true>(I[i]) : bp::from_int32_alu<32, false>(I[i]);
+  }
+}
+
 void h_from_quire(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* out) {
   for (size_t i = 0; i < n; ++i) {
     bp::quire256 q{{w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]}};

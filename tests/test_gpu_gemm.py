@@ -75,6 +75,48 @@ def test_gemm_tc_tile_widths(cuda_lib, path):
     _check_all(777, 257, 2064, path=path, row_major=True)
 
 
+def _check_single(M, N, K, tail, row_major, seed=3):
+    """Every single-output epilogue of the CTA-pair kernel (bposit32 truncate
+    and RTNE, fp32/bf16 dequant, bposit16, INT32), with the last wave cut
+    into whole, half or quarter tiles."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((M, K), seed)
+    B = _rand_i8((N, K), seed + 1)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) * 3 + 0.01
+    ws = torch.rand(N, dtype=torch.float32) * 2 + 0.01
+    Ad, Bd, xd, wd = A.cuda(), B.cuda(), xs.cuda(), ws.cuda()
+    kw = dict(row_major=row_major, path=5, tail=tail)
+    y = O.dequant(acc, xs.numpy(), ws.numpy())
+    for rt in (False, True):
+        r = ops.gemm_i8(Ad, Bd, bp32=True, rtne32=rt, **kw)
+        want = O.encode_int_array(acc, 0, 32, "rtne" if rt else "truncate")
+        assert np.array_equal(_np(r["bp32"], np.uint32), want), (M, N, K, tail, rt)
+    r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.float32, x_scale=xd, w_scale=wd, **kw)
+    assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), (M, N, K, tail)
+    r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.bfloat16, x_scale=xd, w_scale=wd, **kw)
+    assert np.array_equal(_np(r["y"].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y))
+    r = ops.gemm_i8(Ad, Bd, bp32=False, bp16=True, **kw)
+    assert np.array_equal(_np(r["bp16"], np.uint16), O.encode_int_array(acc, 0, 16, "truncate"))
+    r = ops.gemm_i8(Ad, Bd, bp32=False, i32=True, **kw)
+    assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+    assert _api.last_error() == 0
+
+
+# M % 4 == 0 column-major 4-byte outputs go through TMA stores, the others
+# through direct stores; N ragged against every cut width.
+@pytest.mark.parametrize("tail", [0, 1, 2, 3])
+@pytest.mark.parametrize("M,N,K", [(300, 600, 512), (258, 300, 256), (1024, 1000, 256),
+                                   (2560, 2304, 128)])
+def test_gemm_pair_single_outputs(cuda_lib, M, N, K, tail):
+    _check_single(M, N, K, tail, row_major=False)
+
+
+@pytest.mark.parametrize("tail", [1, 3])
+def test_gemm_pair_single_outputs_row_major(cuda_lib, tail):
+    _check_single(516, 777, 384, tail, row_major=True)
+
+
 def test_gemm_row_major_outputs(cuda_lib):
     _check_all(200, 300, 256, row_major=True)
 

@@ -59,9 +59,11 @@ def test_int32_fast_path(hlib):
             assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
 
 
-def test_int32_table_path(hlib):
-    """The epilogue's table-driven encoder equals the oracle on every scale
-    (each power of two and its neighbours) and on random values."""
+@pytest.mark.parametrize("fn", ["h_from_int32_tab", "h_from_int32_alu"])
+def test_int32_table_path(hlib, fn):
+    """The epilogue's table-driven and register-only encoders equal the oracle
+    on every scale (each power of two and its neighbours) and on random
+    values."""
     rng = np.random.default_rng(15)
     edges = []
     for b in range(31):
@@ -74,9 +76,9 @@ def test_int32_table_path(hlib):
     for nb in (16, 32):
         for rtne in (0, 1):
             out = np.empty(I.size, dtype=np.uint32)
-            hlib.h_from_int32_tab(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out))
+            getattr(hlib, fn)(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out))
             exp = O.encode_int_array(I.astype(np.int64), 0, nb, "rtne" if rtne else "truncate")
-            assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
+            assert np.array_equal(out, exp.astype(np.uint32)), (fn, nb, rtne)
 
 
 def test_quire_encoders(hlib, golden):
