@@ -120,7 +120,7 @@ BP_HD uint32_t from_int32(int32_t I, bool rtne) {
 
 // Table-driven INT32 -> bposit for the GEMM epilogue.  For lz = clz(|I|)
 // the regime, exponent and fraction width depend only on lz, so a 33-entry
-// table (lz = 0..32, 32 meaning I == 0) holds
+// table, entry lz + 1 for lz = 0..31 and entry 0 for I == 0, holds
 //   prefix = (regime | e << fw) ^ 1 << fw   and   sh = 31 - fw;
 // with x = |I| << lz (leading one at bit 31), x >> sh puts the leading one at
 // bit fw and the kept fraction below it, and prefix ^ (x >> sh) clears the
@@ -133,9 +133,10 @@ struct I32Entry {
 };
 
 template <int NBITS>
-BP_HD I32Entry i32_table_entry(int lz) {
+BP_HD I32Entry i32_table_entry(int idx) {
   constexpr int N1 = NBITS - 1;
-  if (lz >= 32) return I32Entry{0u, 31u};
+  const int lz = idx - 1;
+  if (lz < 0 || lz >= 32) return I32Entry{0u, 31u};     // I == 0: x = 0, field 0
   const int msb = 31 - lz;
   const int k = msb >> 3, e = msb & 7;
   const int fw = N1 - 5 - k;
@@ -143,15 +144,43 @@ BP_HD I32Entry i32_table_entry(int lz) {
   return I32Entry{(regime | ((uint32_t)e << fw)) ^ (1u << fw), (uint32_t)(31 - fw)};
 }
 
+// clz(a) for a != 0, -1 for a == 0 (one bit-find on the GPU).
+BP_HD int clz_or_m1(uint32_t a) {
+#if defined(__CUDA_ARCH__)
+  int r;
+  asm("bfind.shiftamt.u32 %0, %1;" : "=r"(r) : "r"(a));
+  return r;
+#else
+  return a ? __builtin_clz(a) : -1;
+#endif
+}
+
+// a << n and a >> n for n in [0, 31], and 0 for n >= 32 taken as unsigned
+// (PTX clamps the shift amount; n = -1 is 0xFFFFFFFF).
+BP_HD uint32_t shl_clamped(uint32_t a, int n) {
+#if defined(__CUDA_ARCH__)
+  uint32_t r;
+  asm("shl.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(n));
+  return r;
+#else
+  return (uint32_t)n >= 32u ? 0u : a << n;
+#endif
+}
+
 template <int NBITS, bool RTNE>
 BP_HD uint32_t from_int32_tab(int32_t I, const I32Entry* tab) {
   constexpr int N1 = NBITS - 1;
   constexpr uint32_t FMASK = (1u << N1) - 1u;
   const uint32_t m = (uint32_t)(I >> 31);                // all ones when negative
+#if defined(__CUDA_ARCH__)
+  uint32_t a;                                            // |INT32_MIN| reads as 2^31
+  asm("abs.s32 %0, %1;" : "=r"(a) : "r"(I));
+#else
   const uint32_t a = ((uint32_t)I ^ m) - m;
-  const int lz = clz32(a);
-  const I32Entry t = tab[lz];
-  const uint32_t x = a << (lz & 31);
+#endif
+  const int lz = clz_or_m1(a);
+  const I32Entry t = tab[lz + 1];
+  const uint32_t x = shl_clamped(a, lz);
   uint32_t field = t.prefix ^ (x >> t.sh);
   if (RTNE) {
     const uint32_t rem = x << (32 - t.sh);                // round bit at 31, sticky below
