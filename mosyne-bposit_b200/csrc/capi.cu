@@ -107,6 +107,34 @@ int ensure_scratch(void** ptr, size_t* cur, size_t need) {
 
 namespace {
 
+// Streams and events of the pipelined host-buffer GEMM, per device, made on
+// first use.  Each call returns only after its last download, so the next
+// call's uploads never overwrite staging buffers still in use.
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t up = nullptr, compute = nullptr, down = nullptr;
+  cudaEvent_t uploaded[8] = {}, computed[8] = {};
+};
+HostPipe g_pipe[kMaxDevices];
+std::mutex g_pipe_mu;
+
+HostPipe* host_pipe(int d) {
+  std::lock_guard<std::mutex> lk(g_pipe_mu);
+  HostPipe& h = g_pipe[d];
+  if (!h.ready) {
+    if (cudaStreamCreateWithFlags(&h.up, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h.compute, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h.down, cudaStreamNonBlocking) != cudaSuccess)
+      return nullptr;
+    for (int i = 0; i < 8; ++i)
+      if (cudaEventCreateWithFlags(&h.uploaded[i], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&h.computed[i], cudaEventDisableTiming) != cudaSuccess)
+        return nullptr;
+    h.ready = true;
+  }
+  return &h;
+}
+
 void* stage_buf(int d, int slot, size_t need) {
   HostStage& s = g_stage[d];
   if (ensure_scratch(&s.buf[slot], &s.bytes[slot], need ? need : 1)) return nullptr;
@@ -309,19 +337,42 @@ int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, i
   uint32_t* dbp = out_bp32 ? static_cast<uint32_t*>(stage_buf(d, 2, mn * 4)) : nullptr;
   int32_t* di = out_i32 ? static_cast<int32_t*>(stage_buf(d, 3, mn * 4)) : nullptr;
   if (!dA || !dB || (out_bp32 && !dbp) || (out_i32 && !di)) return RC_ALLOC;
-  cudaStream_t st = 0;
-  if (cudaMemcpyAsync(dA, A, mk, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-      cudaMemcpyAsync(dB, B, nk, cudaMemcpyHostToDevice, st) != cudaSuccess)
-    return RC_LAUNCH;
-  int rc = mosyne_bposit_gemm_i8(dA, dB, M, N, K, nullptr, nullptr, dbp, nullptr, nullptr,
-                                 MOSYNE_DT_F32, di, flags & ~(MOSYNE_XS_SCALAR | MOSYNE_WS_SCALAR),
-                                 nullptr);
-  if (rc) return rc;
-  if (dbp && cudaMemcpyAsync(out_bp32, dbp, mn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-    return RC_LAUNCH;
-  if (di && cudaMemcpyAsync(out_i32, di, mn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-    return RC_LAUNCH;
-  return cudaStreamSynchronize(st) == cudaSuccess ? RC_OK : RC_LAUNCH;
+  HostPipe* hp = host_pipe(d);
+  if (!hp) return RC_LAUNCH;
+  // Pipelined over blocks of output channels: B rows [n0, n1) are contiguous
+  // in B and their outputs are contiguous in the column-major result, so the
+  // upload of block c + 1, the GEMM of block c and the download of block
+  // c - 1 run at the same time (host->device and device->host on their own
+  // copy engines).  A goes up first, whole.
+  const int nblk = N >= 8 * 512 ? 8 : (N >= 2 * 512 ? N / 512 : 1);
+  const int step = ((N + nblk - 1) / nblk + 255) / 256 * 256;
+  const int gflags = flags & ~(MOSYNE_XS_SCALAR | MOSYNE_WS_SCALAR);
+  if (cudaMemcpyAsync(dA, A, mk, cudaMemcpyHostToDevice, hp->up) != cudaSuccess) return RC_LAUNCH;
+  int c = 0;
+  for (int n0 = 0; n0 < N; n0 += step, ++c) {
+    const int nc = N - n0 < step ? N - n0 : step;
+    const size_t boff = (size_t)n0 * K, ooff = (size_t)n0 * M;
+    if (cudaMemcpyAsync(dB + boff, B + boff, (size_t)nc * K, cudaMemcpyHostToDevice, hp->up) !=
+            cudaSuccess ||
+        cudaEventRecord(hp->uploaded[c], hp->up) != cudaSuccess ||
+        cudaStreamWaitEvent(hp->compute, hp->uploaded[c], 0) != cudaSuccess)
+      return RC_LAUNCH;
+    const int rc = mosyne_bposit_gemm_i8(dA, dB + boff, M, nc, K, nullptr, nullptr,
+                                         dbp ? dbp + ooff : nullptr, nullptr, nullptr,
+                                         MOSYNE_DT_F32, di ? di + ooff : nullptr, gflags,
+                                         hp->compute);
+    if (rc) return rc;
+    if (cudaEventRecord(hp->computed[c], hp->compute) != cudaSuccess ||
+        cudaStreamWaitEvent(hp->down, hp->computed[c], 0) != cudaSuccess)
+      return RC_LAUNCH;
+    if (dbp && cudaMemcpyAsync(out_bp32 + ooff, dbp + ooff, (size_t)nc * M * 4,
+                               cudaMemcpyDeviceToHost, hp->down) != cudaSuccess)
+      return RC_LAUNCH;
+    if (di && cudaMemcpyAsync(out_i32 + ooff, di + ooff, (size_t)nc * M * 4,
+                              cudaMemcpyDeviceToHost, hp->down) != cudaSuccess)
+      return RC_LAUNCH;
+  }
+  return cudaStreamSynchronize(hp->down) == cudaSuccess ? RC_OK : RC_LAUNCH;
 }
 
 int mosyne_bposit_linear_w8a8_ex(const void* x, int x_dtype, int M, int K, const int8_t* w_i8,

@@ -190,3 +190,20 @@ def test_gemm_bad_args(cuda_lib):
     assert lib.mosyne_bposit_gemm_i8(a.data_ptr(), a.data_ptr(), 4, 4, 16, 0, 0, 0, 0,
                                      y.data_ptr(), 0, 0, 0, 0) == -20
     assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 3000, 256), (64, 200, 512), (1024, 4096, 128)])
+def test_gemm_host_buffers(cuda_lib, M, N, K):
+    """The host-buffer entry point (uploads, GEMM and downloads pipelined over
+    blocks of output channels) returns the oracle's INT32 and bposit32 codes,
+    column-major [N, M]."""
+    from mosyne_bposit import _api
+    A = _rand_i8((M, K), 11).numpy()
+    B = _rand_i8((N, K), 12).numpy()
+    for rt in (0, _api.RTNE_BP32):
+        bp, i32 = _api.gemm_i8_host(A, B, want_i32=True, flags=rt)
+        acc = O.gemm_exact(A, B.T)
+        assert i32.shape == (M, N) and np.array_equal(i32.astype(np.int64), acc)
+        want = O.encode_int_array(acc, 0, 32, "rtne" if rt else "truncate")
+        assert np.array_equal(np.asarray(bp).view(np.uint32), want)
+    assert _api.last_error() == 0
