@@ -100,6 +100,10 @@ int mosyne_bposit_linear_w8a8_host(const float* host_x, int M, int K, const floa
 #define MOSYNE_OUT_ROW_MAJOR 0x10 /* outputs row-major [M,N] instead of column-major */
 #define MOSYNE_X_ROW_MAJOR 0x20  /* linear: x is row-major [M,K] instead of column-major */
 #define MOSYNE_X_PER_TENSOR 0x40 /* linear: one activation scale for the whole x */
+/* gemm_i8: the bposit outputs encode acc / 2^s (s = 0..31) instead of acc,
+ * the scale_shift of kernels/test_int32_to_bposit32.cu:94-126; the bposit8
+ * path (int8 operands with 6 fraction bits each) uses s = 12. */
+#define MOSYNE_BP_SHIFT(s) ((((unsigned)(s)) & 31u) << 24)
 
 /* Version string of this build. */
 const char* mosyne_bposit_version(void);
@@ -121,6 +125,7 @@ int mosyne_bposit_debug_wait_timeout(unsigned long long limit_ns, mosyne_stream_
  *   acc[m,n] = sum_k A[m,k] * B[n,k]          (exact INT32)
  *   out_bp32 = bposit32(acc)   == quire256_to_bposit32(acc << 96)
  *   out_bp16 = bposit16(acc)
+ *   (acc / 2^s for both with flags MOSYNE_BP_SHIFT(s))
  *   out_f32  = (float)acc / (x_scale[m] * w_scale[n])
  *   out_i32  = acc
  * A is [M,K] with K contiguous; B is [N,K] with K contiguous (= column-major
@@ -204,6 +209,12 @@ int mosyne_bposit_bp16_to_quire(const uint16_t* x, size_t n, mosyne_quire256* ou
 /* kernels/test_int32_to_bposit32.cu:94-126: value = in / 2^scale_shift. */
 int mosyne_bposit_int32_to_bp32(const int32_t* in, size_t n, int scale_shift, uint32_t* out,
                                 int rtne, mosyne_stream_t stream);
+
+/* kernels/test_mera_isometry_imma.cu:43-69, 166-197: bposit8 codes -> int8
+ * fixed point with 6 fraction bits, clamp(floor(value * 64), -128, 127); NaR
+ * and zero give 0.  The decode pass of the bposit8 IMMA path. */
+int mosyne_bposit_bposit8_to_int8(const uint8_t* in, size_t n, int8_t* out,
+                                  mosyne_stream_t stream);
 
 /* kernels/bposit16_reference.py:485-503 (exact value of each binary float):
  * x of dtype MOSYNE_DT_F32 or MOSYNE_DT_F64 -> bposit16 (nbits 16, uint16

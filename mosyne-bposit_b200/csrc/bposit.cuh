@@ -132,15 +132,19 @@ struct I32Entry {
   uint32_t sh;
 };
 
+// `shift` (0..31) encodes I / 2^shift instead of I: the scale becomes
+// msb - shift, which may be negative (regime of -k zeros and a one).
 template <int NBITS>
-BP_HD I32Entry i32_table_entry(int idx) {
+BP_HD I32Entry i32_table_entry(int idx, int shift = 0) {
   constexpr int N1 = NBITS - 1;
   const int lz = idx - 1;
   if (lz < 0 || lz >= 32) return I32Entry{0u, 31u};     // I == 0: x = 0, field 0
-  const int msb = 31 - lz;
-  const int k = msb >> 3, e = msb & 7;
-  const int fw = N1 - 5 - k;
-  const uint32_t regime = ((2u << k) - 1u) << (N1 - 1 - k);
+  const int scale = 31 - lz - shift;
+  const int k = scale >> 3, e = scale & 7;                // floor division
+  const int rlen = k >= 0 ? k + 2 : 1 - k;
+  const int fw = N1 - rlen - 3;
+  const uint32_t regime =
+      k >= 0 ? ((2u << k) - 1u) << (N1 - 1 - k) : 1u << (N1 - 1 + k);
   return I32Entry{(regime | ((uint32_t)e << fw)) ^ (1u << fw), (uint32_t)(31 - fw)};
 }
 
@@ -192,33 +196,46 @@ BP_HD uint32_t from_int32_tab(int32_t I, const I32Entry* tab) {
   return NBITS == 32 ? out : (out & 0xFFFFu);
 }
 
-// The same encoding with the table entry computed in registers: no memory
-// access per value.  The magnitude's leading one sits at bit msb = 31 - lz, so
-// the regime run is k + 1 = (msb >> 3) + 1 ones and the fraction field is
-// fw = NBITS - 6 - k bits wide; x >> sh puts the hidden one at bit fw, where
-// the XOR with (e ^ 1) << fw turns it back into the exponent's low bit.
-template <int NBITS, bool RTNE>
-BP_HD uint32_t from_int32_alu(int32_t I) {
-  constexpr int N1 = NBITS - 1;
-  constexpr uint32_t FMASK = (1u << N1) - 1u;
-  const uint32_t m = (uint32_t)(I >> 31);                // all ones when negative
-  const uint32_t a = ((uint32_t)I ^ m) - m;
-  const int lz = clz32(a);
-  const int msb = 31 - lz;
-  const int k = (msb >> 3) & 3;
-  const int fw = NBITS - 6 - k;
-  const int sh = 37 - NBITS + k;
-  const uint32_t regime = (1u << N1) - ((1u << (N1 - 1)) >> k);
-  const uint32_t x = a << (lz & 31);
-  uint32_t field = (regime | ((uint32_t)((msb & 7) ^ 1) << fw)) ^ (x >> sh);
-  if (RTNE) {
-    const uint32_t rem = x << (32 - sh);                   // round bit at 31, sticky below
-    const uint32_t up = (rem >> 31) & (uint32_t)(((rem << 1) != 0u) | (field & 1u)) &
-                        (uint32_t)(field != FMASK);
-    field += up;
+// ---------------------------------------------------------------------------
+// bposit8 (es = 2, useed = 16, values 2^-24 .. 2^24; kernels/bposit16_reference.py
+// 151-209) -> int8 fixed point with 6 fraction bits, the decode that feeds the
+// bposit8 IMMA path (kernels/test_mera_isometry_imma.cu:43-69, 166-197): the
+// reference takes the code's quire (value x 2^96), shifts it right by 90 bits
+// (floor) and clamps to [-128, 127]; NaR and zero give 0.  Every bposit8 value
+// is a multiple of 2^-24, so the quire is exact and the result is
+// clamp(floor(value * 64)).
+// ---------------------------------------------------------------------------
+BP_HD int8_t bposit8_to_int8(uint32_t code) {
+  code &= 0xFFu;
+  if (code == 0u || code == 0x80u) return 0;
+  const bool neg = (code >> 7) != 0;
+  const uint32_t mag = neg ? ((0u - code) & 0x7Fu) : (code & 0x7Fu);
+  const uint32_t lead = (mag >> 6) & 1u;
+  int run = 1;
+  while (run < 7 && ((mag >> (6 - run)) & 1u) == lead) ++run;
+  int k, e = 0, fw = 0;
+  uint32_t frac = 0;
+  if (run == 7) {
+    k = lead ? 6 : -7;
+  } else {
+    k = lead ? run - 1 : -run;
+    const int left = 6 - run;                  // bits after the regime terminator
+    const int ew = left < 2 ? left : 2;
+    e = ew ? (int)(((mag >> (left - ew)) & ((1u << ew) - 1u)) << (2 - ew)) : 0;
+    fw = left - ew;
+    frac = mag & ((1u << fw) - 1u);
   }
-  const uint32_t out = a ? (field ^ m) - m : 0u;
-  return NBITS == 32 ? out : (out & 0xFFFFu);
+  // value * 64 = ((1 << fw) + frac) * 2^(4k + e + 6 - fw)
+  const int64_t m = (int64_t)((1u << fw) + frac);
+  const int sh = 4 * k + e + 6 - fw;
+  int64_t v;
+  if (sh >= 0) {
+    v = sh > 40 ? (int64_t)1 << 40 : m << sh;   // far above the clamp either way
+    if (neg) v = -v;
+  } else {
+    v = neg ? -((m + ((int64_t)1 << -sh) - 1) >> -sh) : (m >> -sh);   // floor
+  }
+  return (int8_t)(v > 127 ? 127 : (v < -128 ? -128 : v));
 }
 
 // ---------------------------------------------------------------------------

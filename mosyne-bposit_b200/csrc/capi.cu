@@ -12,6 +12,7 @@
 #include <mutex>
 
 #include "alu.cuh"
+#include "bp8.cuh"
 #include "bposit.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
@@ -321,6 +322,7 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
   p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
   p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
   p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  p.bp_shift = (flags >> 24) & 31;
   const int path = (flags >> 16) & 0x3F;  // test hook: force a GEMM path / tail cut
   return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
 }
@@ -473,6 +475,14 @@ int mosyne_bposit_int32_to_bp32(const int32_t* in, size_t n, int scale_shift, ui
   if (!ctx) return RC_NOT_INIT;
   if (n && (!in || !out)) return RC_BAD_ARG;
   return int32_to_bp32_run(ctx, in, n, scale_shift, out, rtne, as_stream(stream));
+}
+
+int mosyne_bposit_bposit8_to_int8(const uint8_t* in, size_t n, int8_t* out,
+                                  mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (n && (!in || !out)) return RC_BAD_ARG;
+  return bp8_to_i8_run(in, n, out, ctx->num_sms, as_stream(stream));
 }
 
 int mosyne_bposit_float_to_bposit(const void* x, int dtype, size_t n, void* out, int nbits,

@@ -22,6 +22,7 @@ struct EpiParams {
   int32_t* i32 = nullptr;
   int row_major = 0;
   int rtne32 = 0, rtne16 = 0;
+  int bp_shift = 0;        // bposit outputs encode acc / 2^bp_shift (0..31)
 };
 
 enum GemmPath {

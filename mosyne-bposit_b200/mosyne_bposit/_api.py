@@ -78,6 +78,7 @@ _SIGS = {
     "mosyne_bposit_quire_to_bp32": (_I, [_P, _SZ, _P, _I, _P]),
     "mosyne_bposit_bp16_to_quire": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit_int32_to_bp32": (_I, [_P, _SZ, _I, _P, _I, _P]),
+    "mosyne_bposit_bposit8_to_int8": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit_float_to_bposit": (_I, [_P, _I, _SZ, _P, _I, _I, _P]),
     "mosyne_bposit_epilogue_i32": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
     "mosyne_bposit16_add": (_I, [_P, _P, _SZ, _P, _P]),
@@ -332,6 +333,11 @@ def int32_to_bp32_dev(x: int, n: int, scale_shift: int, out: int, *, rtne: bool 
     lib = _ensure_library()
     _check(lib.mosyne_bposit_int32_to_bp32(x, n, scale_shift, out, int(rtne), stream),
            "mosyne_bposit_int32_to_bp32")
+
+
+def bposit8_to_int8_dev(x: int, n: int, out: int, *, stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_bposit8_to_int8(x, n, out, stream), "mosyne_bposit_bposit8_to_int8")
 
 
 def float_to_bposit_dev(x: int, dtype: int, n: int, out: int, nbits: int = 16, *,

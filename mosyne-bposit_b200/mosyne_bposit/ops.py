@@ -40,12 +40,14 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
             i32: bool = False, y_dtype: torch.dtype | None = None,
             x_scale: torch.Tensor | None = None, w_scale: torch.Tensor | None = None,
             rtne32: bool = False, rtne16: bool = False, row_major: bool = False,
-            out: dict | None = None, path: int = 0, tail: int = 0) -> dict:
+            out: dict | None = None, path: int = 0, tail: int = 0,
+            scale_shift: int = 0) -> dict:
     """Exact ``acc = A @ B^T`` for int8 ``A [M,K]`` and ``B [N,K]`` (both
     K-contiguous) with the requested encodings of every dot product:
     ``bp32``/``bp16`` (bposit of the INT32 value), ``i32``, and ``y`` =
     ``acc / (x_scale[m] * w_scale[n])`` when ``y_dtype`` is given
     (scalar scales broadcast).  ``out`` may pass preallocated tensors.
+    ``scale_shift`` makes the bposit outputs encode ``acc / 2^scale_shift``.
     ``path`` and ``tail`` pin the kernel choice (tests): path 1 tensor cores,
     2/3 one-CTA tiles 128/256 wide, 4 CUDA cores, 5 CTA pairs; tail 1/2/3 cuts
     the CTA-pair kernel's last wave into whole/half/quarter tiles."""
@@ -77,7 +79,9 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
             flags |= _api.WS_SCALAR
         if "y" not in res:
             res["y"] = _out((M, N), y_dtype, dev, row_major)
-    flags |= ((path & 0xF) << 16) | ((tail & 0x3) << 20)
+    if not 0 <= scale_shift <= 31:
+        raise ValueError("scale_shift must be in 0..31")
+    flags |= ((path & 0xF) << 16) | ((tail & 0x3) << 20) | (scale_shift << 24)
     _api.gemm_i8_dev(A.data_ptr(), B.data_ptr(), M, N, K,
                      x_scale=_ptr(x_scale), w_scale=_ptr(w_scale),
                      out_bp32=_ptr(res.get("bp32")), out_bp16=_ptr(res.get("bp16")),
@@ -245,6 +249,30 @@ def int32_to_bp32(x: torch.Tensor, scale_shift: int = 0, *, rtne: bool = False) 
     _api.int32_to_bp32_dev(x.data_ptr(), x.numel(), scale_shift, out.data_ptr(), rtne=rtne,
                            stream=_stream(x))
     return out
+
+
+def bposit8_to_int8(x: torch.Tensor) -> torch.Tensor:
+    """bposit8 codes (uint8 or int8 tensor) -> int8 fixed point with 6
+    fraction bits, clamp(floor(value * 64)) -- the decode pass of the
+    bposit8 IMMA path; the result feeds ``gemm_i8``."""
+    _need_cuda(x)
+    if x.dtype not in (torch.uint8, torch.int8):
+        raise ValueError("bposit8 codes must be uint8 or int8")
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    _api.bposit8_to_int8_dev(x.data_ptr(), x.numel(), out.data_ptr(), stream=_stream(x))
+    return out
+
+
+def gemm_bposit8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, i32: bool = False,
+                 rtne32: bool = False, row_major: bool = False) -> dict:
+    """bposit8 in, bposit32 out (the reference's IMMA path for bposit8
+    tensors, kernels/test_mera_isometry_imma.cu:224-352): ``A [M,K]`` and
+    ``B [N,K]`` bposit8 codes are decoded to int8 with 6 fraction bits, the
+    exact INT32 GEMM runs on the tensor cores and the epilogue encodes
+    ``acc / 2^12`` to bposit32 (``i32`` returns the raw accumulator)."""
+    return gemm_i8(bposit8_to_int8(A), bposit8_to_int8(B), bp32=bp32, i32=i32, rtne32=rtne32,
+                   row_major=row_major, scale_shift=12)
 
 
 def float_to_bposit(x: torch.Tensor, nbits: int = 16, *, rtne: bool = False) -> torch.Tensor:

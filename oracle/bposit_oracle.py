@@ -196,6 +196,26 @@ def bposit8_to_quire(p: int) -> int:
     return int(v * (1 << QUIRE_FRAC_BITS))
 
 
+def bposit8_to_int8(p: int) -> int:
+    """bposit8 -> int8 fixed point, 6 fraction bits, as the reference builds
+    its decode table (kernels/test_mera_isometry_imma.cu:166-197) from the
+    bposit8 quire table words (kernels/build_bposit_luts.py:302-311): the
+    signed high word w[1] (bit 63 forced on when the quire is negative)
+    shifted right by 26 (floor), clamped to [-128, 127]."""
+    w = quire_to_words(bposit8_to_quire(p))
+    hi = w[1] - (1 << 64) if w[1] >> 63 else w[1]
+    if (w[3] >> 63) and hi >= 0:
+        hi -= 1 << 63
+    v = hi >> (QUIRE_FRAC_BITS - 6 - 64)
+    return max(-128, min(127, v))
+
+
+def bposit8_to_int8_array(codes) -> np.ndarray:
+    """Vectorised bposit8_to_int8 over a uint8 array."""
+    tab = np.array([bposit8_to_int8(i) for i in range(256)], dtype=np.int8)
+    return tab[np.asarray(codes, dtype=np.uint8)]
+
+
 def quire_to_bposit(q: int, nbits: int = 16, mode: str = "truncate") -> int:
     """quire256 (signed int, 96 fraction bits) -> bposit.  pyref:616-631
     (bp16), pyref:775-794 (bp32), enc.cuh:113-204 / 221-321 / 333-418."""

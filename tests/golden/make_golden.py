@@ -150,6 +150,26 @@ def headline():
             "n": len(codes), "seed": 0x5EED1234}
 
 
+def bposit8():
+    """bposit8 -> quire table words exactly as kernels/build_bposit_luts.py:302-311
+    bakes them, and the int8 decode table the reference derives from those
+    words (kernels/test_mera_isometry_imma.cu:166-197, restated here: signed
+    w[1], bit 63 forced on for a negative quire, arithmetic shift by 26,
+    clamp to int8)."""
+    words, to_i8 = [], []
+    for i in range(256):
+        q = R.bposit8_to_quire(i)
+        if q < 0:
+            q += 1 << 256
+        w = [(q >> (64 * k)) & 0xFFFFFFFFFFFFFFFF for k in range(4)]
+        words.append([f"{x:016x}" for x in w])
+        hi = w[1] - (1 << 64) if w[1] >> 63 else w[1]
+        if (w[3] >> 63) and hi >= 0:
+            hi -= 1 << 63
+        to_i8.append(max(-128, min(127, hi >> 26)))
+    return {"to_quire_words": words, "to_int8": to_i8}
+
+
 def probe():
     """packages/mosyne_bposit/src/mosyne_bposit/cross_gpu_probe.py:52-57 and
     examples/canonical_probe_references/probe_{3090,5090}_*.json."""
@@ -173,6 +193,7 @@ def main():
     _write("headline.json", headline())
     _write("pyref_samples.json", pyref_samples())
     _write("lut_sha256.json", lut_hashes())
+    _write("bposit8.json", bposit8())
 
 
 if __name__ == "__main__":

@@ -18,11 +18,11 @@ void h_from_int32(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out
     out[i] = nbits == 16 ? bp::from_int32<16>(I[i], rtne) : bp::from_int32<32>(I[i], rtne);
 }
 
-void h_from_int32_tab(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out) {
+void h_from_int32_tab(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out, int shift) {
   bp::I32Entry t16[33], t32[33];
   for (int i = 0; i < 33; ++i) {
-    t16[i] = bp::i32_table_entry<16>(i);
-    t32[i] = bp::i32_table_entry<32>(i);
+    t16[i] = bp::i32_table_entry<16>(i, shift);
+    t32[i] = bp::i32_table_entry<32>(i, shift);
   }
   for (size_t i = 0; i < n; ++i) {
     if (nbits == 16)
@@ -32,13 +32,8 @@ void h_from_int32_tab(const int32_t* I, size_t n, int nbits, int rtne, uint32_t*
   }
 }
 
-void h_from_int32_alu(const int32_t* I, size_t n, int nbits, int rtne, uint32_t* out) {
-  for (size_t i = 0; i < n; ++i) {
-    if (nbits == 16)
-      out[i] = rtne ? bp::from_int32_alu<16, true>(I[i]) : bp::from_int32_alu<16, false>(I[i]);
-    else
-      out[i] = rtne ? bp::from_int32_alu<32, true>(I[i]) : bp::from_int32_alu<32, false>(I[i]);
-  }
+void h_bp8_to_i8(int8_t* out) {
+  for (int i = 0; i < 256; ++i) out[i] = bp::bposit8_to_int8((uint32_t)i);
 }
 
 void h_from_quire(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* out) {

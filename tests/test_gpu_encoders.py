@@ -98,3 +98,26 @@ def test_empty_inputs(cuda_lib):
     z = torch.empty((0,), dtype=torch.int32, device="cuda")
     assert ops.int32_to_bp32(z).numel() == 0
     assert ops.bp16_to_quire(torch.empty((0,), dtype=torch.int16, device="cuda")).shape == (0, 4)
+
+
+def test_bposit8_to_int8(cuda_lib, golden):
+    """bposit8 -> int8 decode: every code against the reference's table, and
+    a large ragged buffer through the vector path (same alignment phase on
+    both sides) and the byte path (different phases)."""
+    from mosyne_bposit import _api, ops
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8).cuda()
+    want = np.array(golden("bposit8.json")["to_int8"], dtype=np.int8)
+    assert np.array_equal(ops.bposit8_to_int8(codes).cpu().numpy(), want)
+    g = torch.Generator(device="cpu").manual_seed(8)
+    n = (1 << 24) + 37
+    big = torch.randint(0, 256, (n + 64,), generator=g, dtype=torch.int32).to(torch.uint8)
+    ref = O.bposit8_to_int8_array(big.numpy())
+    src = big.cuda()
+    out = torch.full((n + 64,), 99, dtype=torch.int8, device="cuda")
+    for si, oi in ((0, 0), (5, 5), (3, 7), (1, 0)):
+        out.fill_(99)
+        _api.bposit8_to_int8_dev(src[si:].data_ptr(), n, out[oi:].data_ptr())
+        got = out.cpu().numpy()
+        assert np.array_equal(got[oi:oi + n], ref[si:si + n]), (si, oi)
+        assert (got[:oi] == 99).all() and (got[oi + n:] == 99).all(), (si, oi)
+    assert _api.last_error() == 0

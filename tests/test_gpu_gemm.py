@@ -207,3 +207,45 @@ def test_gemm_host_buffers(cuda_lib, M, N, K):
         want = O.encode_int_array(acc, 0, 32, "rtne" if rt else "truncate")
         assert np.array_equal(np.asarray(bp).view(np.uint32), want)
     assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("shift", [6, 12, 31])
+def test_gemm_scale_shift(cuda_lib, shift):
+    """bposit outputs of acc / 2^shift (negative scales included) on every
+    path: CTA pair (TMA-store and direct-store epilogues), single CTA, CUDA
+    cores, and the generic multi-output epilogue."""
+    from mosyne_bposit import _api, ops
+    for (M, N, K), path in (((300, 600, 512), 5), ((258, 300, 256), 5), ((64, 200, 160), 0),
+                            ((70, 90, 40), 4)):
+        A = _rand_i8((M, K), shift)
+        B = _rand_i8((N, K), shift + 1)
+        acc = O.gemm_exact(A.numpy(), B.numpy().T)
+        Ad, Bd = A.cuda(), B.cuda()
+        for rt in (False, True):
+            mode = "rtne" if rt else "truncate"
+            r = ops.gemm_i8(Ad, Bd, bp32=True, rtne32=rt, path=path, scale_shift=shift)
+            assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, shift, 32, mode)), \
+                (M, N, K, path, rt)
+            r = ops.gemm_i8(Ad, Bd, bp32=True, bp16=True, i32=True, rtne32=rt, rtne16=rt, path=path,
+                            scale_shift=shift)
+            assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, shift, 32, mode))
+            assert np.array_equal(_np(r["bp16"], np.uint16), O.encode_int_array(acc, shift, 16, mode))
+            assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+    assert _api.last_error() == 0
+
+
+def test_gemm_bposit8_in_bposit32_out(cuda_lib):
+    """bposit8 operands -> int8 decode -> exact GEMM -> bposit32 of acc / 2^12,
+    the reference's bposit8 IMMA pipeline, against the oracle."""
+    from mosyne_bposit import _api, ops
+    g = torch.Generator(device="cpu").manual_seed(88)
+    for M, N, K in ((512, 768, 1024), (37, 50, 64)):
+        A = torch.randint(0, 256, (M, K), generator=g, dtype=torch.int32).to(torch.uint8)
+        B = torch.randint(0, 256, (N, K), generator=g, dtype=torch.int32).to(torch.uint8)
+        r = ops.gemm_bposit8(A.cuda(), B.cuda(), i32=True)
+        a8 = O.bposit8_to_int8_array(A.numpy())
+        b8 = O.bposit8_to_int8_array(B.numpy())
+        acc = O.gemm_exact(a8, b8.T)
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 12, 32))
+    assert _api.last_error() == 0

@@ -59,11 +59,11 @@ def test_int32_fast_path(hlib):
             assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
 
 
-@pytest.mark.parametrize("fn", ["h_from_int32_tab", "h_from_int32_alu"])
-def test_int32_table_path(hlib, fn):
-    """The epilogue's table-driven and register-only encoders equal the oracle
-    on every scale (each power of two and its neighbours) and on random
-    values."""
+@pytest.mark.parametrize("shift", [0, 6, 12, 24, 31])
+def test_int32_table_path(hlib, shift):
+    """The epilogue's table-driven encoder equals the oracle on every scale
+    (each power of two and its neighbours) and on random values, for the
+    plain integer (shift 0) and for I / 2^shift (negative scales)."""
     rng = np.random.default_rng(15)
     edges = []
     for b in range(31):
@@ -76,9 +76,9 @@ def test_int32_table_path(hlib, fn):
     for nb in (16, 32):
         for rtne in (0, 1):
             out = np.empty(I.size, dtype=np.uint32)
-            getattr(hlib, fn)(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out))
-            exp = O.encode_int_array(I.astype(np.int64), 0, nb, "rtne" if rtne else "truncate")
-            assert np.array_equal(out, exp.astype(np.uint32)), (fn, nb, rtne)
+            hlib.h_from_int32_tab(_p(I), ctypes.c_size_t(I.size), nb, rtne, _p(out), shift)
+            exp = O.encode_int_array(I.astype(np.int64), shift, nb, "rtne" if rtne else "truncate")
+            assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne, shift)
 
 
 def test_quire_encoders(hlib, golden):
@@ -124,3 +124,11 @@ def test_headline_sum(hlib, golden):
     w = np.empty(4, dtype=np.uint64)
     hlib.h_quire_sum(_p(codes), ctypes.c_size_t(codes.size), _p(w))
     assert [f"{int(x):016x}" for x in w] == golden("headline.json")["quire_words"]
+
+
+def test_bposit8_to_int8_table(hlib, golden):
+    """The library's bposit8 decode (built on the host, uploaded with each
+    launch) equals the reference's table for all 256 codes."""
+    out = np.zeros(256, dtype=np.int8)
+    hlib.h_bp8_to_i8(_p(out))
+    assert out.tolist() == golden("bposit8.json")["to_int8"]

@@ -190,3 +190,14 @@ def test_exact_sum_inputs_are_rtne():
     for x, c in zip(v[:200], codes[:200]):
         assert int(c) == O.encode_fraction(Fraction(float(x)), 16, "rtne")
     assert math.isfinite(float(np.abs(v).max()))
+
+
+def test_bposit8_tables(golden):
+    """bposit8 -> quire words (build_bposit_luts.py:302-311 via pyref) and the
+    int8 decode table derived from them (test_mera_isometry_imma.cu:166-197)."""
+    g = golden("bposit8.json")
+    for i in range(256):
+        w = O.quire_to_words(O.bposit8_to_quire(i))
+        assert [f"{x:016x}" for x in w] == g["to_quire_words"][i], i
+        assert O.bposit8_to_int8(i) == g["to_int8"][i], i
+    assert O.bposit8_to_int8(0x40) == 64                  # 1.0 -> 2^6
