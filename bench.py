@@ -168,6 +168,93 @@ def _time_gemm(M, N, K, steps, warmup, dist, seed, lib_call):
     return ms, nsets, out
 
 
+def _events_ms(fn, steps, warmup):
+    """Average device time (ms) of fn() over `steps` back-to-back calls on
+    the current stream, after `warmup` calls."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def extra_workloads(steps, warmup, peaks):
+    """The other measured rows of the path, each on inputs larger than L2
+    where the roofline is HBM (rotating copies otherwise):
+    * C1 linear: 128x2048x11008 W8A8 with a per-tensor activation scale,
+      fp32 y and bposit32 outputs (HBM-bound: weights dominate);
+    * C2 exact sum: 2^24 bposit16 values -> quire256 -> bposit16 (HBM-bound);
+    * the W8A8 SwiGLU FFN of a 3B model at M=2048 (2048 -> 11008 -> 2048):
+      quantise, fused gate/up GEMM with the activation in its epilogue,
+      re-quantise, down GEMM (tensor-bound; torch bf16 FFN timed beside it)."""
+    import torch
+
+    from mosyne_bposit import ops
+    out = {}
+    hbm = peaks["hbm"]
+    # C1 -- rotate weight copies so each call reads its weights from HBM
+    M, K, N = 128, 2048, 11008
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    nw = max(2, math.ceil(3 * L2_BYTES / (N * K)))
+    ws = []
+    for _ in range(nw):
+        w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+        ws.append(ops.quantize_per_channel(w))
+    it = [0]
+
+    def c1():
+        wq, sc = ws[it[0] % nw]
+        it[0] += 1
+        ops.linear_w8a8(x, wq, sc, out_dtype=torch.float32, bp32=True, per_tensor=True)
+    ms = _events_ms(c1, steps, warmup)
+    nbytes = M * K * 4 + N * K + N * 4 + M * N * 4 * 2
+    out["linear_c1_128x2048x11008_per_tensor"] = {
+        "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "achieved_gbs": nbytes / ms / 1e6,
+        "frac_of_hbm": nbytes / ms / 1e6 / hbm, "bound": "hbm",
+        "outputs": "fp32 y + bposit32, row-major", "weight_copies": nw}
+    del ws
+    # C2 -- 2^24 codes (32 MiB), rotated over > 3x L2
+    n = 1 << 24
+    nc = max(2, math.ceil(3 * L2_BYTES / (2 * n)))
+    codes = [torch.randint(-32767, 32768, (n,), device="cuda", generator=g, dtype=torch.int32)
+             .to(torch.int16) for _ in range(nc)]
+    it[0] = 0
+
+    def c2():
+        ops.quire_sum_bp16(codes[it[0] % nc])
+        it[0] += 1
+    ms = _events_ms(c2, steps, warmup)
+    out["exact_sum_c2_2^24_bposit16"] = {
+        "us_per_call": ms * 1e3, "bytes_per_call": 2 * n, "achieved_gbs": 2 * n / ms / 1e6,
+        "frac_of_hbm": 2 * n / ms / 1e6 / hbm, "bound": "hbm", "input_copies": nc}
+    del codes
+    # C4 3B FFN
+    M, D, F = 2048, 2048, 11008
+    xf = torch.randn(M, D, device="cuda", generator=g)
+    wg = torch.randn(F, D, device="cuda", generator=g) * 0.02
+    wu = torch.randn(F, D, device="cuda", generator=g) * 0.02
+    wd = torch.randn(D, F, device="cuda", generator=g) * 0.02
+    packed = ops.pack_swiglu_weights(wg, wu, wd)
+    ms = _events_ms(lambda: ops.ffn_swiglu_w8a8(xf, packed, out_dtype=torch.float32), steps, warmup)
+    xb, wgb, wub, wdb = xf.bfloat16(), wg.bfloat16(), wu.bfloat16(), wd.bfloat16()
+    F_ = torch.nn.functional
+    bms = _events_ms(lambda: F_.linear(F_.silu(F_.linear(xb, wgb)) * F_.linear(xb, wub), wdb),
+                     steps, warmup)
+    ffn_ops = 2.0 * M * D * F * 3
+    out["ffn_swiglu_3b_2048x2048x11008"] = {
+        "us_per_call": ms * 1e3, "tpops": ffn_ops / ms / 1e9,
+        "frac_of_int8_peak": ffn_ops / ms / 1e9 / (2.0 * peaks["bf16"]), "bound": "tensor",
+        "torch_bf16_us_per_call": bms * 1e3, "launches_per_call": 4}
+    return out
+
+
 def _ours(A, B, out, stream, lib, flags=0):
     M, K = A.shape
     N = B.shape[0]
@@ -355,6 +442,7 @@ def run_ours(args):
     }
     line["e2e"] = e2e
     if ws == 1:
+        line["workloads"].update(extra_workloads(args.steps, args.warmup, peaks))
         line["cpu_baseline"] = cpu_baseline(M, N, K)
     print(json.dumps(line), flush=True)
     if dist is not None:

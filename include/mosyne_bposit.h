@@ -210,6 +210,25 @@ int mosyne_bposit_bp16_to_quire(const uint16_t* x, size_t n, mosyne_quire256* ou
 int mosyne_bposit_int32_to_bp32(const int32_t* in, size_t n, int scale_shift, uint32_t* out,
                                 int rtne, mosyne_stream_t stream);
 
+/* The W8A8 SwiGLU FFN of kernels/test_ffn_layer_real_qwen.cu:300-334
+ * (per-token int8 x, gate and up IMMA + dequant, silu(gate) * up in fp32 with
+ * silu(v) = v / (1 + expf(-v)), per-token re-quantisation, down IMMA +
+ * dequant) in four launches:
+ *   x       row-major [M, D] (MOSYNE_DT_F32/BF16/F16)
+ *   w_gu_i8 [2F, D] int8 (K contiguous): gate and up weights quantised per
+ *           channel and interleaved in blocks of 32 channels -- rows
+ *           64b .. 64b+31 are gate channels 32b .. 32b+31, rows 64b+32 ..
+ *           64b+63 the same up channels; w_gu_scale [2F] likewise
+ *   w_down_i8 [D, F] int8 (K contiguous), w_down_scale [D]
+ *   y       row-major [M, D] of y_dtype
+ *   act     optional fp32 row-major [M, F] output of the activation (NULL:
+ *           library scratch)
+ * F must be a multiple of 32 and D, F multiples of 16.  flags: reserved (0). */
+int mosyne_bposit_ffn_swiglu_w8a8(const void* x, int x_dtype, int M, int D,
+                                  const int8_t* w_gu_i8, const float* w_gu_scale, int F,
+                                  const int8_t* w_down_i8, const float* w_down_scale, void* y,
+                                  int y_dtype, float* act, int flags, mosyne_stream_t stream);
+
 /* kernels/test_mera_isometry_imma.cu:43-69, 166-197: bposit8 codes -> int8
  * fixed point with 6 fraction bits, clamp(floor(value * 64), -128, 127); NaR
  * and zero give 0.  The decode pass of the bposit8 IMMA path. */

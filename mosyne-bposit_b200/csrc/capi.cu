@@ -52,6 +52,10 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.partials);
   cudaFree(c.ticket);
   cudaFree(c.lut);
+  cudaFree(c.ffn_act);
+  cudaFree(c.ffn_h_i8);
+  cudaFree(c.ffn_h_scale);
+  cudaFree(c.ffn_amax);
   c = DeviceContext();
 }
 
@@ -375,6 +379,63 @@ int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, i
       return RC_LAUNCH;
   }
   return cudaStreamSynchronize(hp->down) == cudaSuccess ? RC_OK : RC_LAUNCH;
+}
+
+int mosyne_bposit_ffn_swiglu_w8a8(const void* x, int x_dtype, int M, int D,
+                                  const int8_t* w_gu_i8, const float* w_gu_scale, int F,
+                                  const int8_t* w_down_i8, const float* w_down_scale, void* y,
+                                  int y_dtype, float* act, int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || D <= 0 || F <= 0 || (F % 32) != 0 || !x || !w_gu_i8 || !w_gu_scale ||
+      !w_down_i8 || !w_down_scale || !y || !dtype_ok(x_dtype) || !dtype_ok(y_dtype))
+    return RC_BAD_ARG;
+  if ((D % 16) != 0 || (F % 16) != 0) return RC_BAD_ARG;   // TMA row strides
+  cudaStream_t st = as_stream(stream);
+  const size_t mf = (size_t)M * F;
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->x_scale), &ctx->x_scale_bytes, M * sizeof(float)) ||
+      ensure_scratch(reinterpret_cast<void**>(&ctx->x_i8), &ctx->x_i8_bytes, (size_t)M * D) ||
+      (!act && ensure_scratch(reinterpret_cast<void**>(&ctx->ffn_act), &ctx->ffn_act_bytes,
+                              mf * sizeof(float))) ||
+      ensure_scratch(reinterpret_cast<void**>(&ctx->ffn_h_i8), &ctx->ffn_h_i8_bytes, mf) ||
+      ensure_scratch(reinterpret_cast<void**>(&ctx->ffn_h_scale), &ctx->ffn_h_scale_bytes,
+                     M * sizeof(float)) ||
+      ensure_scratch(reinterpret_cast<void**>(&ctx->ffn_amax), &ctx->ffn_amax_bytes,
+                     M * sizeof(uint32_t)))
+    return RC_ALLOC;
+  float* a = act ? act : ctx->ffn_act;
+  // 1. per-token int8 of x (row-major [M, D])
+  int rc = quant_activation(ctx, x_dtype, x, M, D, ctx->x_i8, ctx->x_scale, true, false, st);
+  if (rc) return rc == RC_ALLOC ? RC_ALLOC : RC_LAUNCH;
+  // 2. gate and up in one GEMM (N = 2F, interleaved channel blocks); the
+  //    epilogue writes silu(gate) * up and each row's |max|
+  if (cudaMemsetAsync(ctx->ffn_amax, 0, M * sizeof(uint32_t), st) != cudaSuccess) return RC_LAUNCH;
+  EpiParams p;
+  p.M = M;
+  p.N = 2 * F;
+  p.xs = ctx->x_scale;
+  p.ws = w_gu_scale;
+  p.y = a;
+  p.y_dtype = MOSYNE_DT_F32;
+  p.row_major = 1;
+  p.act_amax = ctx->ffn_amax;
+  rc = gemm_i8_run(ctx->x_i8, w_gu_i8, D, p, ctx, st);
+  if (rc) return rc == RC_BAD_ARG ? RC_BAD_ARG : RC_GEMM;
+  // 3. per-token int8 of the activation with those maxima
+  rc = quant_rows_given_amax(a, M, F, ctx->ffn_amax, ctx->ffn_h_i8, ctx->ffn_h_scale, st);
+  if (rc) return RC_LAUNCH;
+  // 4. down projection, dequantised into y (row-major [M, D])
+  EpiParams q;
+  q.M = M;
+  q.N = D;
+  q.xs = ctx->ffn_h_scale;
+  q.ws = w_down_scale;
+  q.y = y;
+  q.y_dtype = y_dtype;
+  q.row_major = 1;
+  (void)flags;
+  rc = gemm_i8_run(ctx->ffn_h_i8, w_down_i8, F, q, ctx, st);
+  return rc == RC_BAD_ARG ? RC_BAD_ARG : (rc ? RC_GEMM : RC_OK);
 }
 
 int mosyne_bposit_linear_w8a8_ex(const void* x, int x_dtype, int M, int K, const int8_t* w_i8,

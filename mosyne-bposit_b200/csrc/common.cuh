@@ -28,6 +28,16 @@ struct DeviceContext {
   void* partials = nullptr;        // exact-sum block partials
   size_t partials_bytes = 0;
   unsigned int* ticket = nullptr;  // last-block ticket for grid reductions
+  // SwiGLU FFN intermediates: activation [M,F] fp32, its int8 codes, scales
+  // and row maxima
+  float* ffn_act = nullptr;
+  size_t ffn_act_bytes = 0;
+  int8_t* ffn_h_i8 = nullptr;
+  size_t ffn_h_i8_bytes = 0;
+  float* ffn_h_scale = nullptr;
+  size_t ffn_h_scale_bytes = 0;
+  uint32_t* ffn_amax = nullptr;
+  size_t ffn_amax_bytes = 0;
   // bposit16 ALU tables, 65,536 x u16 each, device resident
   uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]
 };

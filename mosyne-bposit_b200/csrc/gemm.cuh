@@ -23,6 +23,11 @@ struct EpiParams {
   int row_major = 0;
   int rtne32 = 0, rtne16 = 0;
   int bp_shift = 0;        // bposit outputs encode acc / 2^bp_shift (0..31)
+  // SwiGLU mode (set together with an fp32 y): the N columns come in blocks of
+  // 64, 32 gate channels then the same 32 up channels; y receives the
+  // row-major [M, N/2] activation silu(gate) * up and act_amax[m] the bit
+  // pattern of max |activation| of row m (atomicMax; must start at zero).
+  uint32_t* act_amax = nullptr;
 };
 
 enum GemmPath {

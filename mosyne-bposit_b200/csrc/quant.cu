@@ -320,6 +320,12 @@ int quant_given_t(const void* x, int M, int K, const float* row_max, int8_t* q, 
   return launch_rc();
 }
 
+int quant_rows_given_amax(const float* x, int R, int C, const uint32_t* amax, int8_t* q,
+                          float* scale, cudaStream_t st) {
+  if (R <= 0 || C <= 0) return RC_BAD_ARG;
+  return quant_rows_t<float>(x, R, C, q, scale, amax, st, 1);
+}
+
 int quant_with_max(int dtype, const void* x, int M, int K, const float* row_max, int8_t* q,
                    float* scale, bool row_major, cudaStream_t st) {
   if (M <= 0 || K <= 0) return RC_BAD_ARG;

@@ -29,4 +29,9 @@ int quant_per_token_colmajor_into(int dtype, const void* x, int M, int K, int8_t
 
 int write_scalar_scale(const uint32_t* amax, float* scale, cudaStream_t st);
 
+// Row-major fp32 rows [R, C] -> int8 with scale[r] = 127 / max, the maxima
+// given as fp32 bit patterns (e.g. accumulated by a GEMM epilogue).
+int quant_rows_given_amax(const float* x, int R, int C, const uint32_t* amax, int8_t* q,
+                          float* scale, cudaStream_t st);
+
 }  // namespace mb

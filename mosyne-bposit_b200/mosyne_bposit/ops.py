@@ -264,6 +264,50 @@ def bposit8_to_int8(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def pack_swiglu_weights(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor) -> dict:
+    """Quantise an FFN's ``nn.Linear`` weights per output channel for
+    ``ffn_swiglu_w8a8``: gate and up ``[F, D]`` are interleaved in blocks of 32
+    channels into one ``[2F, D]`` int8 matrix (and ``[2F]`` scales) so a
+    single GEMM produces both; down ``[D, F]`` is quantised as is."""
+    _need_cuda(w_gate, w_up, w_down)
+    F, D = w_gate.shape
+    if w_up.shape != (F, D) or w_down.shape != (D, F):
+        raise ValueError("expected w_gate, w_up [F, D] and w_down [D, F]")
+    if F % 32:
+        raise ValueError("F must be a multiple of 32")
+    qg, sg = quantize_per_channel(w_gate)
+    qu, su = quantize_per_channel(w_up)
+    qd, sd = quantize_per_channel(w_down)
+    w_gu = torch.stack((qg.view(F // 32, 32, D), qu.view(F // 32, 32, D)), 1).reshape(2 * F, D)
+    s_gu = torch.stack((sg.view(F // 32, 32), su.view(F // 32, 32)), 1).reshape(2 * F)
+    return {"w_gu_i8": w_gu.contiguous(), "w_gu_scale": s_gu.contiguous(), "w_down_i8": qd,
+            "w_down_scale": sd, "F": F, "D": D}
+
+
+def ffn_swiglu_w8a8(x: torch.Tensor, packed: dict, *, out_dtype: torch.dtype | None = None,
+                    act: torch.Tensor | None = None) -> torch.Tensor:
+    """W8A8 SwiGLU FFN ``down(silu(gate(x)) * up(x))`` on row-major ``x [M, D]``
+    with weights from ``pack_swiglu_weights``; ``act`` (fp32 ``[M, F]``) may
+    receive the activation.  Returns ``y [M, D]`` in ``out_dtype`` (default
+    ``x.dtype``)."""
+    _need_cuda(x)
+    x = x.contiguous()
+    M, D = x.shape
+    if D != packed["D"]:
+        raise ValueError(f"x has {D} features, the FFN expects {packed['D']}")
+    F = packed["F"]
+    out_dtype = out_dtype or x.dtype
+    y = torch.empty((M, D), dtype=out_dtype, device=x.device)
+    if act is not None and (act.dtype != torch.float32 or act.shape != (M, F) or
+                            not act.is_contiguous()):
+        raise ValueError("act must be a contiguous fp32 [M, F] tensor")
+    _api.ffn_swiglu_w8a8_dev(x.data_ptr(), _DT[x.dtype], M, D, packed["w_gu_i8"].data_ptr(),
+                             packed["w_gu_scale"].data_ptr(), F, packed["w_down_i8"].data_ptr(),
+                             packed["w_down_scale"].data_ptr(), y.data_ptr(), _DT[out_dtype],
+                             act=act.data_ptr() if act is not None else 0, stream=_stream(x))
+    return y
+
+
 def gemm_bposit8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, i32: bool = False,
                  rtne32: bool = False, row_major: bool = False) -> dict:
     """bposit8 in, bposit32 out (the reference's IMMA path for bposit8

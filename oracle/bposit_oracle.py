@@ -420,6 +420,33 @@ def dequant(acc: np.ndarray, xs: np.ndarray, ws: np.ndarray) -> np.ndarray:
     return (np.asarray(acc).astype(np.float32) / den).astype(np.float32)
 
 
+def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    """``silu(g) * u`` with ``silu(v) = v / (1 + exp(-v))`` in fp32
+    (kernels/test_ffn_layer_real_qwen.cu:101-108).  The reference evaluates
+    CUDA's ``expf``; numpy's float32 ``exp`` may differ from it in the last
+    place, so this stage is compared within a tolerance."""
+    g = np.asarray(g, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        e = np.exp(-g).astype(np.float32)
+    return ((g / (np.float32(1) + e)).astype(np.float32) * np.asarray(u, np.float32)).astype(np.float32)
+
+
+def ffn_swiglu_w8a8(x: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, w_down: np.ndarray):
+    """The W8A8 SwiGLU FFN of kernels/test_ffn_layer_real_qwen.cu:300-334 on
+    row-major x [M, D] and nn.Linear weights (gate/up [F, D], down [D, F]).
+    Returns (y, act, xq, xs) with every stage in fp32 as the reference does."""
+    xq, xs = quant_per_token(x)
+    gq, gs = quant_per_channel(np.asarray(w_gate, np.float32).T)
+    uq, us = quant_per_channel(np.asarray(w_up, np.float32).T)
+    dq, ds = quant_per_channel(np.asarray(w_down, np.float32).T)
+    g = dequant(gemm_exact(xq, gq), xs, gs)
+    u = dequant(gemm_exact(xq, uq), xs, us)
+    act = swiglu(g, u)
+    hq, hs = quant_per_token(act)
+    y = dequant(gemm_exact(hq, dq), hs, ds)
+    return y, act, xq, xs
+
+
 def f32_to_bf16_bits(y: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even fp32 -> bf16 bit pattern (``__float2bfloat16``)."""
     u = np.ascontiguousarray(y, dtype=np.float32).view(np.uint32).astype(np.uint64)

@@ -96,6 +96,9 @@ def _check_single(M, N, K, tail, row_major, seed=3):
     assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), (M, N, K, tail)
     r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.bfloat16, x_scale=xd, w_scale=wd, **kw)
     assert np.array_equal(_np(r["y"].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y))
+    r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.float16, x_scale=xd, w_scale=wd, **kw)
+    with np.errstate(over="ignore"):
+        assert np.array_equal(_np(r["y"]).view(np.uint16), y.astype(np.float16).view(np.uint16))
     r = ops.gemm_i8(Ad, Bd, bp32=False, bp16=True, **kw)
     assert np.array_equal(_np(r["bp16"], np.uint16), O.encode_int_array(acc, 0, 16, "truncate"))
     r = ops.gemm_i8(Ad, Bd, bp32=False, i32=True, **kw)
@@ -112,9 +115,13 @@ def test_gemm_pair_single_outputs(cuda_lib, M, N, K, tail):
     _check_single(M, N, K, tail, row_major=False)
 
 
-@pytest.mark.parametrize("tail", [1, 3])
-def test_gemm_pair_single_outputs_row_major(cuda_lib, tail):
-    _check_single(516, 777, 384, tail, row_major=True)
+# row-major outputs: N % 8 == 0 takes TMA stores for 4- and 2-byte outputs,
+# N % 4 == 0 for 4-byte ones only, other N direct stores
+@pytest.mark.parametrize("tail", [1, 2, 3])
+@pytest.mark.parametrize("M,N,K", [(516, 777, 384), (516, 776, 384), (300, 1000, 256),
+                                   (2560, 2304, 128), (257, 1028, 128)])
+def test_gemm_pair_single_outputs_row_major(cuda_lib, M, N, K, tail):
+    _check_single(M, N, K, tail, row_major=True)
 
 
 def test_gemm_row_major_outputs(cuda_lib):
