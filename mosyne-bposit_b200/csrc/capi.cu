@@ -56,6 +56,8 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.ffn_h_i8);
   cudaFree(c.ffn_h_scale);
   cudaFree(c.ffn_amax);
+  cudaFree(c.splitk_ws);
+  cudaFree(c.splitk_cnt);
   c = DeviceContext();
 }
 
@@ -327,7 +329,8 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
   p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
   p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
   p.bp_shift = (flags >> 24) & 31;
-  const int path = (flags >> 16) & 0x3F;  // test hook: force a GEMM path / tail cut
+  // test hooks: force a GEMM path / tail cut (bits 16-21) / K slices (bits 29-31)
+  const int path = ((flags >> 16) & 0x3F) | ((int)(((unsigned)flags >> 29) & 0x7u) << 8);
   return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
 }
 
@@ -409,7 +412,7 @@ int mosyne_bposit_ffn_swiglu_w8a8(const void* x, int x_dtype, int M, int D,
   if (rc) return rc == RC_ALLOC ? RC_ALLOC : RC_LAUNCH;
   // 2. gate and up in one GEMM (N = 2F, interleaved channel blocks); the
   //    epilogue writes silu(gate) * up and each row's |max|
-  if (cudaMemsetAsync(ctx->ffn_amax, 0, M * sizeof(uint32_t), st) != cudaSuccess) return RC_LAUNCH;
+  if (zero_words_run(ctx->ffn_amax, (size_t)M, st) != RC_OK) return RC_LAUNCH;
   EpiParams p;
   p.M = M;
   p.N = 2 * F;

@@ -48,6 +48,10 @@ int epilogue_i32_run(const int32_t* acc, const EpiParams& p, DeviceContext* ctx,
                      cudaStream_t st);
 
 // Bounded wait that nothing satisfies; sets the device error word.
+// n 32-bit words of device memory set to zero by a kernel (orders correctly
+// before the programmatic-dependent GEMM launches, unlike a memset node).
+int zero_words_run(uint32_t* p, size_t n, cudaStream_t st);
+
 int debug_wait_run(unsigned long long limit_ns, DeviceContext* ctx, cudaStream_t st);
 
 }  // namespace mb

@@ -97,6 +97,7 @@ extern "C" int mosyne_bposit_linear_w8a8_noalloc(const float* x, int M, int K, c
   ctx.device = dev;
   ctx.num_sms = d->num_sms;
   ctx.err = nullptr;             // no error word: device waits stay bounded, give-ups are silent
+  ctx.scratch_ok = false;        // no split-K workspace: one K slice per tile
   EpiParams p;
   p.M = M;
   p.N = N;

@@ -84,6 +84,58 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   }
 }
 
+// One block per contiguous row, for few and long rows (activations of a few
+// hundred tokens): block-wide max, then quantise.  `given_amax` as above;
+// `scalar_scale` (nullable) receives the per-tensor scale from row 0.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) quant_row_block_kernel(
+    const T* __restrict__ x, int C, int8_t* __restrict__ q, float* __restrict__ scale,
+    const uint32_t* __restrict__ given_amax, int amax_stride, float* __restrict__ scalar_scale) {
+  constexpr int V = Vec<T>::N;
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const T* xr = x + (size_t)row * C;
+  int8_t* qr = q + (size_t)row * C;
+  float m = 0.f;
+  if (given_amax) {
+    m = __uint_as_float(given_amax[(size_t)row * amax_stride]);
+  } else {
+    if (VEC) {
+      for (int c = threadIdx.x * V; c < C; c += 256 * V) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+        const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32<T>(v[i])));
+      }
+    } else {
+      for (int c = threadIdx.x; c < C; c += 256) m = fmaxf(m, fabsf(to_f32<T>(xr[c])));
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
+              fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+  }
+  const float s = quant_scale_from_max(m);
+  if (threadIdx.x == 0) {
+    if (scale) scale[row] = s;
+    if (scalar_scale && row == 0) *scalar_scale = s;
+  }
+  if (VEC) {
+    for (int c = threadIdx.x * V; c < C; c += 256 * V) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+      const T* v = reinterpret_cast<const T*>(&raw);
+      int8_t o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = quantize1(to_f32<T>(v[i]), s);
+      if (V == 4) *reinterpret_cast<uint32_t*>(qr + c) = *reinterpret_cast<uint32_t*>(o);
+      else *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<uint2*>(o);
+    }
+  } else {
+    for (int c = threadIdx.x; c < C; c += 256) qr[c] = quantize1(to_f32<T>(xr[c]), s);
+  }
+}
+
 // Column-major x [M,K] (m contiguous): per-row |max| via coalesced reads of
 // 64 consecutive rows, reduced with atomicMax on the fp32 bit pattern (exact
 // and order independent for non-negative values).
@@ -199,11 +251,24 @@ __global__ void __launch_bounds__(256) rowmax_rows_kernel(const T* __restrict__ 
   if (lane == 0) amax[row] = __float_as_uint(m);
 }
 
+// Rows per launch below which each row gets a whole block instead of a warp
+// (a warp per row would leave most SMs idle).
+constexpr int kBlockPerRowMax = 2048;
+
 template <typename T>
 int quant_rows_t(const void* x, int R, int C, int8_t* q, float* scale, const uint32_t* amax,
-                 cudaStream_t st, int amax_stride = 0) {
+                 cudaStream_t st, int amax_stride = 0, float* scalar_scale = nullptr) {
   constexpr int V = Vec<T>::N;
   const bool vec = (C % V == 0) && aligned16<T>(x) && ((reinterpret_cast<uintptr_t>(q) % V) == 0);
+  if (R <= kBlockPerRowMax || scalar_scale) {
+    if (vec)
+      quant_row_block_kernel<T, true><<<(unsigned)R, 256, 0, st>>>(
+          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale);
+    else
+      quant_row_block_kernel<T, false><<<(unsigned)R, 256, 0, st>>>(
+          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale);
+    return launch_rc();
+  }
   const unsigned blocks = (unsigned)((R + 7) / 8);
   if (vec)
     quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
@@ -249,11 +314,8 @@ int per_tensor_t(DeviceContext* ctx, const void* t, int rows, int cols, int8_t* 
     absmax_kernel<T, 1><<<blocks, 256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
   int rc = launch_rc();
   if (rc) return rc;
-  if (row_major) {
-    rc = quant_rows_t<T>(t, rows, cols, q, nullptr, ctx->amax, st);
-    if (rc) return rc;
-    return write_scalar_scale(ctx->amax, scale, st);
-  }
+  if (row_major)   // the quantiser's row 0 also writes the per-tensor scale
+    return quant_rows_t<T>(t, rows, cols, q, nullptr, ctx->amax, st, 0, scale);
   colmajor_quant_kernel<T><<<dim3((rows + 63) / 64, (cols + 63) / 64), 256, 0, st>>>(
       static_cast<const T*>(t), rows, cols, ctx->amax, 0, q, scale);
   return launch_rc();

@@ -4,11 +4,12 @@
 // (kernels/test_determinism_headline.cu:65-91, <<<1,32>>>, which is only
 // correct for one warp) and the <=32-block entropy reduction
 // (kernels/shannon_entropy_bposit16.cu:45-119) with a grid-wide one:
-// 16-byte loads of 8 codes, arithmetic bposit16 -> fixed-point decode
-// (no 2 MiB table), a per-thread 256-bit accumulator updated with add.cc
-// chains, warp shuffles, a shared-memory block step, per-block partials and
-// a last-block finish.  Integer addition is associative, so the quire (and
-// every encoding of it) is identical for any grid, schedule or GPU.
+// 16-byte streaming loads of 8 codes, an arithmetic bposit16 decode (no
+// 2 MiB table) into per-regime int64 sums kept in shared memory, folded once
+// per thread into a 256-bit quire, then warp shuffles, a shared-memory block
+// step, per-block partials and a last-block finish.  Integer addition is
+// associative, so the quire (and every encoding of it) is identical for any
+// grid, schedule or GPU.
 #include "bposit.cuh"
 #include "common.cuh"
 #include "quire.cuh"
@@ -29,6 +30,55 @@ __device__ __forceinline__ void q_accumulate_bp16(quire256& acc, uint32_t code) 
   }
   const quire256 t = bp::q_from_shifted(m, sh);
   acc = d.neg ? bp::q_sub(acc, t) : bp::q_add(acc, t);
+}
+
+// Per-regime integer sums.  A bposit16 code with regime run length rs
+// (k = rs - 1 for a run of ones, -rs for zeros) has value
+//   mant * 2^(8k + e - fw),   fw = max(0, 11 - rs),
+// with the exponent bits e and the fraction width fixed by rs.  So within one
+// regime v = mant << e (< 2^18) carries the whole value, and the regime's sum
+// is an ordinary integer sum of v.  Each thread keeps one int64 sum per
+// regime k = -12 .. 14 (exact for 2^45 values) in its own shared-memory
+// column and folds them into the quire once at the end: S_k << (8k - fw + 96),
+// mod 2^256 like the quire itself.  Regimes k < -12 lie below 2^-96 for every
+// code and add nothing, as in the per-value conversion (which truncates there).
+// Every code takes the same path: no divergence on rare regimes.
+constexpr int kGroups = 27;
+constexpr int kGroupLow = -12;
+
+__device__ __forceinline__ void group_accumulate_bp16(long long* g, int stride, uint32_t code) {
+  const uint32_t p = code & 0xFFFFu;
+  const uint32_t neg = p >> 15;
+  const uint32_t rest = neg ? ((0u - p) & 0x7FFFu) : p;   // zero and NaR: rest == 0
+  const uint32_t lead = (rest >> 14) & 1u;
+  const uint32_t x = lead ? (~rest & 0x7FFFu) : rest;
+  const int rs = __clz(x) - 17;                           // regime run length, 1..15
+  const int k = lead ? rs - 1 : -rs;
+  if (rest == 0u || k < kGroupLow) return;
+  const int rem = rs < 14 ? 14 - rs : 0;                  // bits after the terminator
+  const int ew = rem < 3 ? rem : 3;
+  const int fw = rem - ew;
+  const uint32_t e = ((rest >> fw) & ((1u << ew) - 1u)) << (3 - ew);
+  const uint32_t mant = (1u << fw) | (rest & ((1u << fw) - 1u));
+  const long long v = (long long)(mant << e);
+  long long* slot = g + (k - kGroupLow) * stride;
+  *slot += neg ? -v : v;
+}
+
+__device__ __forceinline__ quire256 groups_to_quire(const long long* g, int stride, quire256 q) {
+#pragma unroll 1
+  for (int i = 0; i < kGroups; ++i) {
+    const long long s = g[i * stride];
+    if (s == 0) continue;
+    const int k = i + kGroupLow;
+    const int rs = k >= 0 ? k + 1 : -k;
+    const int fw = rs < 11 ? 11 - rs : 0;
+    const int sh = 8 * k - fw + bp::kQuireFracBits;     // 0 .. 208
+    const uint64_t mag = s < 0 ? (uint64_t)(-s) : (uint64_t)s;
+    const quire256 t = bp::q_from_shifted(mag, sh);
+    q = s < 0 ? bp::q_sub(q, t) : bp::q_add(q, t);
+  }
+  return q;
 }
 
 __device__ __forceinline__ quire256 shfl_down_q(const quire256& q, int off) {
@@ -59,6 +109,10 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
   __shared__ bool is_last;
+  extern __shared__ long long groups[];                   // [kGroups][256]
+  long long* g = groups + threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < kGroups; ++i) g[i * 256] = 0;
   quire256 acc = bp::q_zero();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -68,17 +122,18 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     const size_t nv = n / 8;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     for (size_t i = tid; i < nv; i += stride) {
-      const uint4 r = __ldg(xv + i);
+      const uint4 r = __ldcs(xv + i);
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        q_accumulate_bp16(acc, w[j] & 0xFFFFu);
-        q_accumulate_bp16(acc, w[j] >> 16);
+        group_accumulate_bp16(g, 256, w[j] & 0xFFFFu);
+        group_accumulate_bp16(g, 256, w[j] >> 16);
       }
     }
     done = nv * 8;
   }
-  for (size_t i = done + tid; i < n; i += stride) q_accumulate_bp16(acc, x[i]);
+  for (size_t i = done + tid; i < n; i += stride) group_accumulate_bp16(g, 256, x[i]);
+  acc = groups_to_quire(g, 256, acc);
 
   acc = block_reduce_q(acc, sh);
   if (threadIdx.x == 0) {
@@ -173,7 +228,15 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
   if (blocks == 0) blocks = 1;
   if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
     return RC_ALLOC;
-  quire_sum_bp16_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+  constexpr int kSumSmem = kGroups * 256 * sizeof(long long);   // 54 KiB: 4 blocks per SM
+  static bool attr_done[kMaxDevices] = {};
+  if (!attr_done[ctx->device]) {
+    if (cudaFuncSetAttribute(quire_sum_bp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSumSmem) != cudaSuccess)
+      return RC_LAUNCH;
+    attr_done[ctx->device] = true;
+  }
+  quire_sum_bp16_kernel<<<(unsigned)blocks, 256, kSumSmem, st>>>(
       x, n, static_cast<quire256*>(ctx->partials), ctx->ticket,
       reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
       (flags & MOSYNE_RTNE_BP32) != 0);

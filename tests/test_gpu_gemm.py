@@ -256,3 +256,54 @@ def test_gemm_bposit8_in_bposit32_out(cuda_lib):
         assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
         assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 12, 32))
     assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("split", [2, 3, 5])
+@pytest.mark.parametrize("M,N,K,path", [(128, 1100, 2048, 3), (77, 600, 1040, 2), (300, 520, 1536, 3)])
+def test_gemm_single_cta_split_k(cuda_lib, M, N, K, path, split):
+    """Single-CTA kernel with K cut into slices whose exact INT32 partials the
+    last slice of each tile combines: every output kind, both layouts."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((M, K), split)
+    B = _rand_i8((N, K), split + 10)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) * 3 + 0.01
+    ws = torch.rand(N, dtype=torch.float32) * 2 + 0.01
+    y = O.dequant(acc, xs.numpy(), ws.numpy())
+    Ad, Bd, xd, wd = A.cuda(), B.cuda(), xs.cuda(), ws.cuda()
+    for rm in (False, True):
+        kw = dict(row_major=rm, path=path, split=split)
+        r = ops.gemm_i8(Ad, Bd, bp32=True, **kw)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32)), (rm,)
+        r = ops.gemm_i8(Ad, Bd, bp32=True, y_dtype=torch.float32, x_scale=xd, w_scale=wd, **kw)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+        assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32))
+        r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.bfloat16, x_scale=xd, w_scale=wd, **kw)
+        assert np.array_equal(_np(r["y"].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y))
+        r = ops.gemm_i8(Ad, Bd, bp32=True, bp16=True, i32=True, rtne32=True, **kw)
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32, "rtne"))
+    # repeated calls reuse the arrival counters
+    for _ in range(3):
+        r = ops.gemm_i8(Ad, Bd, bp32=False, i32=True, path=path, split=split)
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+    assert _api.last_error() == 0
+
+
+def test_gemm_fp32_and_bposit32_outputs(cuda_lib):
+    """The two-output epilogue (fp32 dequant + bposit32 of the same dot
+    products) on both kernels and layouts."""
+    from mosyne_bposit import _api, ops
+    for (M, N, K), path in (((300, 1000, 512), 5), ((96, 1000, 512), 0), ((128, 11008, 2048), 0)):
+        A = _rand_i8((M, K), 4)
+        B = _rand_i8((N, K), 5)
+        acc = O.gemm_exact(A.numpy(), B.numpy().T)
+        xs = torch.rand(M, dtype=torch.float32) + 0.5
+        ws = torch.rand(N, dtype=torch.float32) + 0.5
+        y = O.dequant(acc, xs.numpy(), ws.numpy())
+        for rm in (False, True):
+            r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=True, y_dtype=torch.float32, x_scale=xs.cuda(),
+                            w_scale=ws.cuda(), row_major=rm, path=path)
+            assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32)), (M, rm)
+            assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), (M, rm)
+    assert _api.last_error() == 0
