@@ -32,50 +32,49 @@ __device__ __forceinline__ void q_accumulate_bp16(quire256& acc, uint32_t code) 
   acc = d.neg ? bp::q_sub(acc, t) : bp::q_add(acc, t);
 }
 
-// Per-regime integer sums.  A bposit16 code with regime run length rs
-// (k = rs - 1 for a run of ones, -rs for zeros) has value
-//   mant * 2^(8k + e - fw),   fw = max(0, 11 - rs),
-// with the exponent bits e and the fraction width fixed by rs.  So within one
-// regime v = mant << e (< 2^18) carries the whole value, and the regime's sum
-// is an ordinary integer sum of v.  Each thread keeps one int64 sum per
-// regime k = -12 .. 14 (exact for 2^45 values) in its own shared-memory
-// column and folds them into the quire once at the end: S_k << (8k - fw + 96),
-// mod 2^256 like the quire itself.  Regimes k < -12 lie below 2^-96 for every
-// code and add nothing, as in the per-value conversion (which truncates there).
-// Every code takes the same path: no divergence on rare regimes.
+// Per-regime integer sums.  For a bposit16 code with regime run length rs
+// (k = rs - 1 for a run of ones, -rs for zeros), shifting the 15-bit
+// magnitude left by 17 + rs + 1 leaves the exponent e in the top three bits
+// and the fraction left-aligned below it, so W = 1.f as an integer with 11
+// fraction bits (2^11 + f * 2^(11 - fw)) and
+//   value * 2^96 = (W << e) * 2^(8k + 85).
+// Within one regime the whole value is therefore V = W << e (< 2^19), and the
+// regime's sum is an ordinary integer sum of V.  Each thread keeps one int32
+// sum per regime k = -12 .. 14 in its own shared-memory column (exact for
+// 4096 values; folded into the 256-bit quire every 2048 values and at the
+// end), the decode is branch-free and the same for every code.  Regimes
+// k < -12 lie below 2^-96 and add nothing, as in the per-value conversion
+// (which truncates there); for k = -12 and -11 every V is a multiple of the
+// 2^11 / 2^3 the fold divides out, so the sum stays exact.
 constexpr int kGroups = 27;
 constexpr int kGroupLow = -12;
+constexpr int kFoldIters = 256;                          // x 8 codes per iteration
 
-__device__ __forceinline__ void group_accumulate_bp16(long long* g, int stride, uint32_t code) {
-  const uint32_t p = code & 0xFFFFu;
-  const uint32_t neg = p >> 15;
-  const uint32_t rest = neg ? ((0u - p) & 0x7FFFu) : p;   // zero and NaR: rest == 0
-  const uint32_t lead = (rest >> 14) & 1u;
-  const uint32_t x = lead ? (~rest & 0x7FFFu) : rest;
-  const int rs = __clz(x) - 17;                           // regime run length, 1..15
-  const int k = lead ? rs - 1 : -rs;
-  if (rest == 0u || k < kGroupLow) return;
-  const int rem = rs < 14 ? 14 - rs : 0;                  // bits after the terminator
-  const int ew = rem < 3 ? rem : 3;
-  const int fw = rem - ew;
-  const uint32_t e = ((rest >> fw) & ((1u << ew) - 1u)) << (3 - ew);
-  const uint32_t mant = (1u << fw) | (rest & ((1u << fw) - 1u));
-  const long long v = (long long)(mant << e);
-  long long* slot = g + (k - kGroupLow) * stride;
-  *slot += neg ? -v : v;
+__device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
+  const uint32_t rest = (uint32_t)abs(code_sext) & 0x7FFFu;   // zero and NaR: 0
+  const uint32_t y = rest << 17;
+  const int rs = __clz(y ^ (y << 1)) + 1;                 // regime run length
+  const uint32_t z = y << ((rs + 1) & 31);
+  const uint32_t e = z >> 29;
+  const int V = (int)(((((z >> 18) & 0x7FFu) | 0x800u)) << e);
+  const int k = (int)y < 0 ? rs - 1 : -rs;
+  if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * 256, code_sext < 0 ? -V : V);
 }
 
-__device__ __forceinline__ quire256 groups_to_quire(const long long* g, int stride, quire256 q) {
+__device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
 #pragma unroll 1
   for (int i = 0; i < kGroups; ++i) {
-    const long long s = g[i * stride];
+    const int s = g[i * 256];
     if (s == 0) continue;
-    const int k = i + kGroupLow;
-    const int rs = k >= 0 ? k + 1 : -k;
-    const int fw = rs < 11 ? 11 - rs : 0;
-    const int sh = 8 * k - fw + bp::kQuireFracBits;     // 0 .. 208
-    const uint64_t mag = s < 0 ? (uint64_t)(-s) : (uint64_t)s;
-    const quire256 t = bp::q_from_shifted(mag, sh);
+    g[i * 256] = 0;
+    const int sh = 8 * (i + kGroupLow) + 85;              // -11 .. 197
+    uint64_t mag = s < 0 ? (uint64_t)(-(long long)s) : (uint64_t)s;
+    int shp = sh;
+    if (shp < 0) {
+      mag >>= -shp;                                       // exact: every V is a multiple
+      shp = 0;
+    }
+    const quire256 t = bp::q_from_shifted(mag, shp);
     q = s < 0 ? bp::q_sub(q, t) : bp::q_add(q, t);
   }
   return q;
@@ -109,8 +108,8 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
   __shared__ bool is_last;
-  extern __shared__ long long groups[];                   // [kGroups][256]
-  long long* g = groups + threadIdx.x;
+  extern __shared__ int groups[];                         // [kGroups][256]
+  int* g = groups + threadIdx.x;
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) g[i * 256] = 0;
   quire256 acc = bp::q_zero();
@@ -121,19 +120,24 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
   if (vec) {
     const size_t nv = n / 8;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
+    int iters = 0;
     for (size_t i = tid; i < nv; i += stride) {
       const uint4 r = __ldcs(xv + i);
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        group_accumulate_bp16(g, 256, w[j] & 0xFFFFu);
-        group_accumulate_bp16(g, 256, w[j] >> 16);
+        group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
+        group_accumulate_bp16(g, (int)w[j] >> 16);
+      }
+      if (++iters == kFoldIters) {
+        acc = fold_groups(g, acc);
+        iters = 0;
       }
     }
     done = nv * 8;
   }
-  for (size_t i = done + tid; i < n; i += stride) group_accumulate_bp16(g, 256, x[i]);
-  acc = groups_to_quire(g, 256, acc);
+  for (size_t i = done + tid; i < n; i += stride) group_accumulate_bp16(g, (int)(int16_t)x[i]);
+  acc = fold_groups(g, acc);
 
   acc = block_reduce_q(acc, sh);
   if (threadIdx.x == 0) {
@@ -222,13 +226,13 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
                        int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
   size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
-  size_t cap = (size_t)ctx->num_sms * 4;
+  size_t cap = (size_t)ctx->num_sms * 8;     // 8 blocks of 27 KiB shared memory per SM
   if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
     return RC_ALLOC;
-  constexpr int kSumSmem = kGroups * 256 * sizeof(long long);   // 54 KiB: 4 blocks per SM
+  constexpr int kSumSmem = kGroups * 256 * sizeof(int);         // 27 KiB
   static bool attr_done[kMaxDevices] = {};
   if (!attr_done[ctx->device]) {
     if (cudaFuncSetAttribute(quire_sum_bp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
