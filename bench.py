@@ -262,6 +262,21 @@ def extra_workloads(steps, warmup, peaks):
         "inputs": "+-2^U, U ~ Uniform[-24, 24], bposit16 RTNE",
         "timing": "CUDA-graph replay of the calls"}
     del codes
+    # C4 QK^T: 32 heads x (2048 x 2048 x 128), fp32 scores + bposit32 codes
+    # (output-bound: 1 GiB written per call)
+    H, S_, D_ = 32, 2048, 128
+    q = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
+    k = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
+    qs = torch.rand(H, S_, device="cuda", generator=g) + 0.5
+    kscale = torch.rand(H, S_, device="cuda", generator=g) + 0.5
+    ms = _events_ms(lambda: ops.gemm_i8_batched(q, k, bp32=True, y_dtype=torch.float32,
+                                                x_scale=qs, w_scale=kscale), steps, warmup)
+    qk_bytes = 2 * H * S_ * D_ + 2 * H * S_ * 4 + H * S_ * S_ * 8
+    out["qkt_32x2048x2048x128_fp32_bposit32"] = {
+        "us_per_call": ms * 1e3, "bytes_per_call": qk_bytes, "achieved_gbs": qk_bytes / ms / 1e6,
+        "frac_of_hbm": qk_bytes / ms / 1e6 / hbm, "bound": "hbm",
+        "tpops": 2.0 * H * S_ * S_ * D_ / ms / 1e9, "launches_per_call": H}
+    del q, k
     # C4 3B FFN
     M, D, F = 2048, 2048, 11008
     xf = torch.randn(M, D, device="cuda", generator=g)

@@ -137,6 +137,18 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
                           uint16_t* out_bp16, void* out_y, int y_dtype, int32_t* out_i32,
                           int flags, mosyne_stream_t stream);
 
+/* A batch of independent GEMMs of the same shape (attention scores Q K^T
+ * per head: kernels/test_ffn_layer_* shapes of the C4 QK^T workload):
+ * A [batch][M][K], B [batch][N][K] (K contiguous), x_scale [batch][M] and
+ * w_scale [batch][N] (or single values with the SCALAR flags), each output
+ * [batch] x ([M,N] column- or row-major) contiguous per batch entry.  Same
+ * outputs and flags as mosyne_bposit_gemm_i8 for every entry. */
+int mosyne_bposit_gemm_i8_batched(const int8_t* A, const int8_t* B, int batch, int M, int N,
+                                  int K, const float* x_scale, const float* w_scale,
+                                  uint32_t* out_bp32, uint16_t* out_bp16, void* out_y,
+                                  int y_dtype, int32_t* out_i32, int flags,
+                                  mosyne_stream_t stream);
+
 /* Host-buffer round trip of mosyne_bposit_gemm_i8 (A, B and outputs in host
  * memory; synchronous), the end-to-end form of the GEMM. */
 int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, int K,

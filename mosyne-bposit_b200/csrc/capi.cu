@@ -334,6 +334,54 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
   return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
 }
 
+int mosyne_bposit_gemm_i8_batched(const int8_t* A, const int8_t* B, int batch, int M, int N,
+                                  int K, const float* x_scale, const float* w_scale,
+                                  uint32_t* out_bp32, uint16_t* out_bp16, void* out_y,
+                                  int y_dtype, int32_t* out_i32, int flags,
+                                  mosyne_stream_t stream) {
+  if (batch < 0 || M <= 0 || N <= 0 || K <= 0) return RC_BAD_ARG;
+  if (batch == 0) return RC_OK;
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (!A || !B || (out_y && (!x_scale || !w_scale || !dtype_ok(y_dtype)))) return RC_BAD_ARG;
+  {
+    EpiParams p;
+    p.M = M;
+    p.N = N;
+    p.batch = batch;
+    p.xs = x_scale;
+    p.ws = w_scale;
+    p.xs_stride = (flags & MOSYNE_XS_SCALAR) ? 0 : 1;
+    p.ws_stride = (flags & MOSYNE_WS_SCALAR) ? 0 : 1;
+    p.bp32 = out_bp32;
+    p.bp16 = out_bp16;
+    p.y = out_y;
+    p.y_dtype = y_dtype;
+    p.i32 = out_i32;
+    p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+    p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+    p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+    p.bp_shift = (flags >> 24) & 31;
+    if (gemm_i8_batched_fused(A, B, K, p, ctx, as_stream(stream)) == RC_OK) return RC_OK;
+  }
+  // Otherwise one launch per entry, back to back on one stream: each is
+  // launched as a programmatic dependent, so its set-up overlaps the
+  // previous one's tail.
+  const size_t mk = (size_t)M * K, nk = (size_t)N * K, mn = (size_t)M * N;
+  const size_t ysz = y_dtype == MOSYNE_DT_F32 ? 4 : 2;
+  const bool xs1 = (flags & MOSYNE_XS_SCALAR) != 0, ws1 = (flags & MOSYNE_WS_SCALAR) != 0;
+  for (int b = 0; b < batch; ++b) {
+    const int rc = mosyne_bposit_gemm_i8(
+        A + b * mk, B + b * nk, M, N, K, x_scale ? x_scale + (xs1 ? 0 : (size_t)b * M) : nullptr,
+        w_scale ? w_scale + (ws1 ? 0 : (size_t)b * N) : nullptr,
+        out_bp32 ? out_bp32 + b * mn : nullptr, out_bp16 ? out_bp16 + b * mn : nullptr,
+        out_y ? static_cast<char*>(out_y) + b * mn * ysz : nullptr, y_dtype,
+        out_i32 ? out_i32 + b * mn : nullptr, flags, stream);
+    if (rc) return rc;
+  }
+  return RC_OK;
+}
+
 int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, int K,
                                uint32_t* out_bp32, int32_t* out_i32, int flags) {
   DeviceContext* ctx = ctx_get_or_init();

@@ -28,6 +28,9 @@ struct EpiParams {
   // row-major [M, N/2] activation silu(gate) * up and act_amax[m] the bit
   // pattern of max |activation| of row m (atomicMax; must start at zero).
   uint32_t* act_amax = nullptr;
+  // Batched GEMM (CTA-pair kernel with TMA-store outputs only): A [batch][M][K],
+  // B [batch][N][K], outputs and scales contiguous per entry.
+  int batch = 1;
 };
 
 enum GemmPath {
@@ -51,6 +54,11 @@ int epilogue_i32_run(const int32_t* acc, const EpiParams& p, DeviceContext* ctx,
 // n 32-bit words of device memory set to zero by a kernel (orders correctly
 // before the programmatic-dependent GEMM launches, unlike a memset node).
 int zero_words_run(uint32_t* p, size_t n, cudaStream_t st);
+
+// All p.batch entries in one CTA-pair launch; RC_BAD_ARG when the shape or the
+// outputs need the per-entry path (the caller then launches entry by entry).
+int gemm_i8_batched_fused(const int8_t* A, const int8_t* B, int K, const EpiParams& p,
+                          DeviceContext* ctx, cudaStream_t st);
 
 int debug_wait_run(unsigned long long limit_ns, DeviceContext* ctx, cudaStream_t st);
 

@@ -66,6 +66,8 @@ _SIGS = {
     "mosyne_bposit_debug_wait_timeout": (_I, [ctypes.c_ulonglong, _P]),
     "mosyne_bposit_gemm_i8": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P]),
     "mosyne_bposit_gemm_i8_host": (_I, [_P, _P, _I, _I, _I, _P, _P, _I]),
+    "mosyne_bposit_gemm_i8_batched": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P,
+                                           _I, _P]),
     "mosyne_bposit_linear_w8a8_ex": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _I, _P, _P, _I, _P]),
     "mosyne_bposit_quantize_per_token": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "mosyne_bposit_quantize_per_tensor": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
@@ -240,6 +242,18 @@ def gemm_i8_dev(A: int, B: int, M: int, N: int, K: int, *, x_scale: int = 0, w_s
     lib = _ensure_library()
     _check(lib.mosyne_bposit_gemm_i8(A, B, M, N, K, x_scale, w_scale, out_bp32, out_bp16, out_y,
                                      y_dtype, out_i32, flags, stream), "mosyne_bposit_gemm_i8")
+
+
+def gemm_i8_batched_dev(A: int, B: int, batch: int, M: int, N: int, K: int, *, x_scale: int = 0,
+                        w_scale: int = 0, out_bp32: int = 0, out_bp16: int = 0, out_y: int = 0,
+                        y_dtype: int = DT_F32, out_i32: int = 0, flags: int = 0,
+                        stream: int = 0) -> None:
+    """``batch`` independent fused GEMMs of one shape, operands and outputs
+    contiguous per batch entry."""
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_gemm_i8_batched(A, B, batch, M, N, K, x_scale, w_scale, out_bp32,
+                                             out_bp16, out_y, y_dtype, out_i32, flags, stream),
+           "mosyne_bposit_gemm_i8_batched")
 
 
 def gemm_i8_host(A: np.ndarray, B: np.ndarray, *, want_i32: bool = False, flags: int = 0):

@@ -95,6 +95,55 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
     return res
 
 
+def gemm_i8_batched(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool = False,
+                    i32: bool = False, y_dtype: torch.dtype | None = None,
+                    x_scale: torch.Tensor | None = None, w_scale: torch.Tensor | None = None,
+                    rtne32: bool = False, rtne16: bool = False,
+                    row_major: bool = False) -> dict:
+    """``gemm_i8`` over a batch (attention scores per head): ``A [b,M,K]``,
+    ``B [b,N,K]``, scales ``[b,M]`` / ``[b,N]`` (or one value); outputs
+    ``[b,M,N]`` (column-major per entry unless ``row_major``)."""
+    _need_cuda(A, B, x_scale, w_scale)
+    if A.dtype != torch.int8 or B.dtype != torch.int8:
+        raise ValueError("A and B must be int8")
+    if A.dim() != 3 or B.dim() != 3 or A.shape[0] != B.shape[0] or A.shape[2] != B.shape[2]:
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)} vs B {tuple(B.shape)}")
+    A = A.contiguous()
+    B = B.contiguous()
+    b, M, K = A.shape
+    N = B.shape[1]
+    dev = A.device
+
+    def out(dtype):
+        if row_major:
+            return torch.empty((b, M, N), dtype=dtype, device=dev)
+        return torch.empty((b, N, M), dtype=dtype, device=dev).transpose(1, 2)
+    res = {}
+    if bp32:
+        res["bp32"] = out(torch.int32)
+    if bp16:
+        res["bp16"] = out(torch.int16)
+    if i32:
+        res["i32"] = out(torch.int32)
+    flags = (_api.RTNE_BP32 if rtne32 else 0) | (_api.RTNE_BP16 if rtne16 else 0) | \
+        (_api.OUT_ROW_MAJOR if row_major else 0)
+    if y_dtype is not None:
+        if x_scale is None or w_scale is None:
+            raise ValueError("dequantised output needs x_scale and w_scale")
+        x_scale, w_scale = x_scale.contiguous(), w_scale.contiguous()
+        if x_scale.numel() == 1:
+            flags |= _api.XS_SCALAR
+        if w_scale.numel() == 1:
+            flags |= _api.WS_SCALAR
+        res["y"] = out(y_dtype)
+    _api.gemm_i8_batched_dev(A.data_ptr(), B.data_ptr(), b, M, N, K, x_scale=_ptr(x_scale),
+                             w_scale=_ptr(w_scale), out_bp32=_ptr(res.get("bp32")),
+                             out_bp16=_ptr(res.get("bp16")), out_y=_ptr(res.get("y")),
+                             y_dtype=_DT[y_dtype] if y_dtype else 0, out_i32=_ptr(res.get("i32")),
+                             flags=flags, stream=_stream(A))
+    return res
+
+
 def quantize_per_token(x: torch.Tensor, *, col_major: bool = False):
     """Per-token int8 quantisation of ``x [M,K]`` -> (``q [M,K]`` K-contiguous,
     ``scale [M]``).  With ``col_major`` the tensor passed is the ``[K, M]``

@@ -307,3 +307,29 @@ def test_gemm_fp32_and_bposit32_outputs(cuda_lib):
             assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32)), (M, rm)
             assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), (M, rm)
     assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("b,M,N,K", [(3, 300, 260, 128), (4, 64, 96, 64), (2, 512, 512, 256)])
+def test_gemm_batched(cuda_lib, b, M, N, K):
+    """Independent GEMMs per batch entry (attention scores per head), every
+    output kind, both layouts, per-entry and scalar scales."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((b, M, K), 21)
+    B = _rand_i8((b, N, K), 22)
+    xs = torch.rand(b, M) + 0.5
+    ws = torch.rand(b, N) + 0.5
+    for rm in (False, True):
+        r = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=True, i32=True, y_dtype=torch.float32,
+                                x_scale=xs.cuda(), w_scale=ws.cuda(), row_major=rm)
+        r2 = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=False, y_dtype=torch.bfloat16,
+                                 x_scale=xs.cuda(), w_scale=torch.tensor([0.75]).cuda(),
+                                 row_major=rm)
+        for h in range(b):
+            acc = O.gemm_exact(A[h].numpy(), B[h].numpy().T)
+            assert np.array_equal(_np(r["i32"][h]).astype(np.int64), acc), (h, rm)
+            assert np.array_equal(_np(r["bp32"][h], np.uint32), O.encode_int_array(acc, 0, 32))
+            y = O.dequant(acc, xs[h].numpy(), ws[h].numpy())
+            assert np.array_equal(_np(r["y"][h]).view(np.uint32), y.view(np.uint32))
+            y2 = O.dequant(acc, xs[h].numpy(), np.full(N, 0.75, np.float32))
+            assert np.array_equal(_np(r2["y"][h].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y2))
+    assert _api.last_error() == 0
