@@ -333,3 +333,33 @@ def test_gemm_batched(cuda_lib, b, M, N, K):
             y2 = O.dequant(acc, xs[h].numpy(), np.full(N, 0.75, np.float32))
             assert np.array_equal(_np(r2["y"][h].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y2))
     assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("b,M,N,K", [(3, 300, 260, 128), (5, 512, 700, 256), (2, 1024, 96, 64)])
+def test_gemm_batched_one_launch(cuda_lib, b, M, N, K):
+    """Batches the CTA-pair kernel takes in one launch (M > 128, one or two
+    TMA-stored outputs): bposit32, fp32 + bposit32, bf16, both layouts where
+    the strides allow TMA stores, per-entry and scalar scales."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((b, M, K), 31)
+    B = _rand_i8((b, N, K), 32)
+    xs = torch.rand(b, M) + 0.5
+    ws = torch.rand(b, N) + 0.5
+    accs = [O.gemm_exact(A[h].numpy(), B[h].numpy().T) for h in range(b)]
+    for rm in (False, True):
+        r = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=True, row_major=rm)
+        r2 = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=True, y_dtype=torch.float32,
+                                 x_scale=xs.cuda(), w_scale=ws.cuda(), row_major=rm)
+        r3 = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=False, y_dtype=torch.bfloat16,
+                                 x_scale=torch.tensor([1.5]).cuda(), w_scale=ws.cuda(),
+                                 row_major=rm)
+        for h in range(b):
+            acc = accs[h]
+            want = O.encode_int_array(acc, 0, 32)
+            assert np.array_equal(_np(r["bp32"][h], np.uint32), want), (h, rm)
+            assert np.array_equal(_np(r2["bp32"][h], np.uint32), want), (h, rm)
+            y = O.dequant(acc, xs[h].numpy(), ws[h].numpy())
+            assert np.array_equal(_np(r2["y"][h]).view(np.uint32), y.view(np.uint32)), (h, rm)
+            y3 = O.dequant(acc, np.full(M, 1.5, np.float32), ws[h].numpy())
+            assert np.array_equal(_np(r3["y"][h].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y3))
+    assert _api.last_error() == 0
