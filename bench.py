@@ -297,6 +297,51 @@ def extra_workloads(steps, warmup, peaks):
     return out
 
 
+def ksplit_workload(dist, ws, steps, warmup):
+    """K-split across the ranks (the exchange the path has): each rank holds a
+    4096-deep K slice of a 4096 x 4096 x (4096 * ranks) GEMM, computes its
+    exact INT32 partial, the partials are summed with an NCCL int32
+    all-reduce (exact: two's-complement addition is associative) and every
+    rank encodes the sum to bposit32.  Times the whole step and the
+    all-reduce alone (CUDA events, slowest rank)."""
+    import torch
+
+    from mosyne_bposit import dist as D
+    M = N = Kr = 4096
+    g = torch.Generator(device="cuda").manual_seed(300 + dist.get_rank())
+    A = torch.randint(-127, 128, (M, Kr), device="cuda", generator=g, dtype=torch.int8)
+    B = torch.randint(-127, 128, (N, Kr), device="cuda", generator=g, dtype=torch.int8)
+    acc = torch.empty((N, M), dtype=torch.int32, device="cuda")
+
+    def step():   # the library's K-split call
+        return D.ksplit_gemm_i8(A, B, bp32=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    dist.barrier()
+    e0.record()
+    for _ in range(steps):
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+    e1.record()
+    torch.cuda.synchronize()
+    ar_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    ops_total = 2.0 * M * N * Kr * ws
+    return {"shape": [M, N, Kr * ws], "ms_per_step": ms, "tpops": ops_total / ms / 1e9,
+            "allreduce_ms": ar_ms, "allreduce_bytes": 4 * M * N,
+            "allreduce_busbw_gbs": 2 * (ws - 1) / ws * 4 * M * N / ar_ms / 1e6,
+            "note": "mosyne_bposit.dist.ksplit_gemm_i8: local GEMM to exact INT32, NCCL int32 "
+                    "all-reduce of the 64 MiB partials, bposit32 epilogue on every rank"}
+
+
 def _ours(A, B, out, stream, lib, flags=0):
     M, K = A.shape
     N = B.shape[0]
@@ -448,6 +493,7 @@ def run_ours(args):
     lib_ms, _, _ = _time_gemm(M, N, K, args.steps, args.warmup, None, 300 + rank, _cublas_i8)
     lib_ms2, _, _ = _time_gemm(M2, N2, K2, args.steps, args.warmup, None, 400 + rank, _cublas_i8)
     e2e = _e2e(M, N, K, max(3, min(args.steps, 10)), lib, dist, ws)
+    ksplit = ksplit_workload(dist, ws, max(3, min(args.steps, 10)), 2) if dist is not None else None
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -483,6 +529,8 @@ def run_ours(args):
         "clocks": clocks,
     }
     line["e2e"] = e2e
+    if ksplit is not None:
+        line["workloads"]["ksplit_4096x4096xK"] = ksplit
     if ws == 1:
         line["workloads"].update(extra_workloads(args.steps, args.warmup, peaks))
         line["cpu_baseline"] = cpu_baseline(M, N, K)
