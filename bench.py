@@ -176,7 +176,9 @@ def _events_ms(fn, steps, warmup, graph=False):
     host-side launch cost are then timed on the device, as a serving loop
     replaying graphs runs them."""
     import torch
-    for _ in range(warmup):
+    # a graph capture cannot allocate: the first call (scratch buffers) runs
+    # before it even with no warm-up requested
+    for _ in range(max(warmup, 1 if graph else 0)):
         fn()
     torch.cuda.synchronize()
     if graph:
@@ -203,98 +205,212 @@ def _events_ms(fn, steps, warmup, graph=False):
     return e0.elapsed_time(e1) / steps
 
 
-def extra_workloads(steps, warmup, peaks):
+def extra_workloads(steps, warmup, peaks, select=None):
     """The other measured rows of the path, each on inputs larger than L2
     where the roofline is HBM (rotating copies otherwise):
-    * C1 linear: 128x2048x11008 W8A8 with a per-tensor activation scale,
+    * c1: W8A8 linear 128x2048x11008 with a per-tensor activation scale,
       fp32 y and bposit32 outputs (HBM-bound: weights dominate);
-    * C2 exact sum: 2^24 bposit16 values -> quire256 -> bposit16 (HBM-bound);
-    * the W8A8 SwiGLU FFN of a 3B model at M=2048 (2048 -> 11008 -> 2048):
+    * c2: exact sum of 2^24 bposit16 values -> quire256 -> bposit16 (HBM-bound);
+    * qkt: 32 heads of 2048x2048x128 QK^T, fp32 scores + bposit32 codes in one
+      batched launch (HBM-bound: 1 GiB written per call);
+    * ffn: the W8A8 SwiGLU FFN of a 3B model at M=2048 (2048 -> 11008 -> 2048):
       quantise, fused gate/up GEMM with the activation in its epilogue,
-      re-quantise, down GEMM (tensor-bound; torch bf16 FFN timed beside it)."""
+      re-quantise, down GEMM (tensor-bound; torch bf16 FFN timed beside it);
+    * bp8: the bposit8 path at 4096^3 -- decode both operands (bposit8 ->
+      int8 fixed point) and one fused GEMM whose epilogue encodes acc / 2^12.
+    ``select`` (a set of those names) limits the run to some of them."""
     import torch
 
     from mosyne_bposit import ops
     out = {}
     hbm = peaks["hbm"]
-    # C1 -- rotate weight copies so each call reads its weights from HBM
-    M, K, N = 128, 2048, 11008
+    want = (lambda k: True) if select is None else (lambda k: k in select)
     g = torch.Generator(device="cuda").manual_seed(0)
-    x = torch.randn(M, K, device="cuda", generator=g)
-    nw = max(2, math.ceil(3 * L2_BYTES / (N * K)))
-    ws = []
-    for _ in range(nw):
-        w = torch.randn(N, K, device="cuda", generator=g) * 0.02
-        ws.append(ops.quantize_per_channel(w))
     it = [0]
+    if want("c1"):
+        # rotate weight copies so each call reads its weights from HBM
+        M, K, N = 128, 2048, 11008
+        x = torch.randn(M, K, device="cuda", generator=g)
+        nw = max(2, math.ceil(3 * L2_BYTES / (N * K)))
+        ws = []
+        for _ in range(nw):
+            w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+            ws.append(ops.quantize_per_channel(w))
 
-    def c1():
-        wq, sc = ws[it[0] % nw]
-        it[0] += 1
-        ops.linear_w8a8(x, wq, sc, out_dtype=torch.float32, bp32=True, per_tensor=True)
-    ms = _events_ms(c1, steps, warmup, graph=True)
-    nbytes = M * K * 4 + N * K + N * 4 + M * N * 4 * 2
-    out["linear_c1_128x2048x11008_per_tensor"] = {
-        "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "achieved_gbs": nbytes / ms / 1e6,
-        "frac_of_hbm": nbytes / ms / 1e6 / hbm, "bound": "hbm",
-        "outputs": "fp32 y + bposit32, row-major", "weight_copies": nw,
-        "timing": "CUDA-graph replay of the calls"}
-    del ws
-    # C2 -- 2^24 codes (32 MiB) of the headline distribution: magnitudes 2^U,
-    # U ~ Uniform[-24, 24], random signs, rounded to bposit16 (RTNE);
-    # rotated over > 3x L2
-    n = 1 << 24
-    nc = max(2, math.ceil(3 * L2_BYTES / (2 * n)))
-    codes = []
-    for _ in range(nc):
-        u = torch.rand(n, device="cuda", generator=g, dtype=torch.float64) * 48.0 - 24.0
-        sgn = torch.where(torch.rand(n, device="cuda", generator=g) < 0.5, -1.0, 1.0).double()
-        codes.append(ops.float_to_bposit(sgn * torch.exp2(u), 16, rtne=True))
-    it[0] = 0
+        def c1():
+            wq, sc = ws[it[0] % nw]
+            it[0] += 1
+            ops.linear_w8a8(x, wq, sc, out_dtype=torch.float32, bp32=True, per_tensor=True)
+        ms = _events_ms(c1, steps, warmup, graph=True)
+        nbytes = M * K * 4 + N * K + N * 4 + M * N * 4 * 2
+        out["linear_c1_128x2048x11008_per_tensor"] = {
+            "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "achieved_gbs": nbytes / ms / 1e6,
+            "frac_of_hbm": nbytes / ms / 1e6 / hbm, "bound": "hbm",
+            "outputs": "fp32 y + bposit32, row-major", "weight_copies": nw,
+            "timing": "CUDA-graph replay of the calls"}
+        del ws
+    if want("c2"):
+        # 2^24 codes (32 MiB) of the headline distribution: magnitudes 2^U,
+        # U ~ Uniform[-24, 24], random signs, rounded to bposit16 (RTNE);
+        # rotated over > 3x L2
+        n = 1 << 24
+        nc = max(2, math.ceil(3 * L2_BYTES / (2 * n)))
+        codes = []
+        for _ in range(nc):
+            u = torch.rand(n, device="cuda", generator=g, dtype=torch.float64) * 48.0 - 24.0
+            sgn = torch.where(torch.rand(n, device="cuda", generator=g) < 0.5, -1.0, 1.0).double()
+            codes.append(ops.float_to_bposit(sgn * torch.exp2(u), 16, rtne=True))
+        it[0] = 0
 
-    def c2():
-        ops.quire_sum_bp16(codes[it[0] % nc])
-        it[0] += 1
-    ms = _events_ms(c2, steps, warmup, graph=True)
-    out["exact_sum_c2_2^24_bposit16"] = {
-        "us_per_call": ms * 1e3, "bytes_per_call": 2 * n, "achieved_gbs": 2 * n / ms / 1e6,
-        "frac_of_hbm": 2 * n / ms / 1e6 / hbm, "bound": "hbm", "input_copies": nc,
-        "inputs": "+-2^U, U ~ Uniform[-24, 24], bposit16 RTNE",
-        "timing": "CUDA-graph replay of the calls"}
-    del codes
-    # C4 QK^T: 32 heads x (2048 x 2048 x 128), fp32 scores + bposit32 codes
-    # (output-bound: 1 GiB written per call)
-    H, S_, D_ = 32, 2048, 128
-    q = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
-    k = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
-    qs = torch.rand(H, S_, device="cuda", generator=g) + 0.5
-    kscale = torch.rand(H, S_, device="cuda", generator=g) + 0.5
-    ms = _events_ms(lambda: ops.gemm_i8_batched(q, k, bp32=True, y_dtype=torch.float32,
-                                                x_scale=qs, w_scale=kscale), steps, warmup)
-    qk_bytes = 2 * H * S_ * D_ + 2 * H * S_ * 4 + H * S_ * S_ * 8
-    out["qkt_32x2048x2048x128_fp32_bposit32"] = {
-        "us_per_call": ms * 1e3, "bytes_per_call": qk_bytes, "achieved_gbs": qk_bytes / ms / 1e6,
-        "frac_of_hbm": qk_bytes / ms / 1e6 / hbm, "bound": "hbm",
-        "tpops": 2.0 * H * S_ * S_ * D_ / ms / 1e9, "launches_per_call": H}
-    del q, k
-    # C4 3B FFN
-    M, D, F = 2048, 2048, 11008
-    xf = torch.randn(M, D, device="cuda", generator=g)
-    wg = torch.randn(F, D, device="cuda", generator=g) * 0.02
-    wu = torch.randn(F, D, device="cuda", generator=g) * 0.02
-    wd = torch.randn(D, F, device="cuda", generator=g) * 0.02
-    packed = ops.pack_swiglu_weights(wg, wu, wd)
-    ms = _events_ms(lambda: ops.ffn_swiglu_w8a8(xf, packed, out_dtype=torch.float32), steps, warmup)
-    xb, wgb, wub, wdb = xf.bfloat16(), wg.bfloat16(), wu.bfloat16(), wd.bfloat16()
-    F_ = torch.nn.functional
-    bms = _events_ms(lambda: F_.linear(F_.silu(F_.linear(xb, wgb)) * F_.linear(xb, wub), wdb),
-                     steps, warmup)
-    ffn_ops = 2.0 * M * D * F * 3
-    out["ffn_swiglu_3b_2048x2048x11008"] = {
-        "us_per_call": ms * 1e3, "tpops": ffn_ops / ms / 1e9,
-        "frac_of_int8_peak": ffn_ops / ms / 1e9 / (2.0 * peaks["bf16"]), "bound": "tensor",
-        "torch_bf16_us_per_call": bms * 1e3, "launches_per_call": 4}
+        def c2():
+            ops.quire_sum_bp16(codes[it[0] % nc])
+            it[0] += 1
+        ms = _events_ms(c2, steps, warmup, graph=True)
+        out["exact_sum_c2_2^24_bposit16"] = {
+            "us_per_call": ms * 1e3, "bytes_per_call": 2 * n, "achieved_gbs": 2 * n / ms / 1e6,
+            "frac_of_hbm": 2 * n / ms / 1e6 / hbm, "bound": "hbm", "input_copies": nc,
+            "inputs": "+-2^U, U ~ Uniform[-24, 24], bposit16 RTNE",
+            "timing": "CUDA-graph replay of the calls"}
+        small = codes[0][: 1 << 16].clone()
+        ms = _events_ms(lambda: ops.quire_sum_bp16(small), steps, warmup, graph=True)
+        out["exact_sum_c2_65536_bposit16"] = {
+            "us_per_call": ms * 1e3, "bytes_per_call": 2 << 16, "bound": "latency",
+            "inputs": "the first 65,536 codes of the 2^24 set",
+            "timing": "CUDA-graph replay of the calls"}
+        del codes
+    if want("qkt"):
+        # 32 heads x (2048 x 2048 x 128), fp32 scores + bposit32 codes
+        # (output-bound: 1 GiB written per call)
+        H, S_, D_ = 32, 2048, 128
+        q = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
+        k = torch.randint(-127, 128, (H, S_, D_), device="cuda", generator=g, dtype=torch.int8)
+        qs = torch.rand(H, S_, device="cuda", generator=g) + 0.5
+        kscale = torch.rand(H, S_, device="cuda", generator=g) + 0.5
+        ms = _events_ms(lambda: ops.gemm_i8_batched(q, k, bp32=True, y_dtype=torch.float32,
+                                                    x_scale=qs, w_scale=kscale), steps, warmup)
+        qk_bytes = 2 * H * S_ * D_ + 2 * H * S_ * 4 + H * S_ * S_ * 8
+        out["qkt_32x2048x2048x128_fp32_bposit32"] = {
+            "us_per_call": ms * 1e3, "bytes_per_call": qk_bytes,
+            "achieved_gbs": qk_bytes / ms / 1e6, "frac_of_hbm": qk_bytes / ms / 1e6 / hbm,
+            "bound": "hbm", "tpops": 2.0 * H * S_ * S_ * D_ / ms / 1e9, "launches_per_call": 1}
+        del q, k
+    if want("ffn"):
+        M, D, F = 2048, 2048, 11008
+        xf = torch.randn(M, D, device="cuda", generator=g)
+        wg = torch.randn(F, D, device="cuda", generator=g) * 0.02
+        wu = torch.randn(F, D, device="cuda", generator=g) * 0.02
+        wd = torch.randn(D, F, device="cuda", generator=g) * 0.02
+        packed = ops.pack_swiglu_weights(wg, wu, wd)
+        ms = _events_ms(lambda: ops.ffn_swiglu_w8a8(xf, packed, out_dtype=torch.float32),
+                        steps, warmup)
+        xb, wgb, wub, wdb = xf.bfloat16(), wg.bfloat16(), wu.bfloat16(), wd.bfloat16()
+        F_ = torch.nn.functional
+        bms = _events_ms(lambda: F_.linear(F_.silu(F_.linear(xb, wgb)) * F_.linear(xb, wub), wdb),
+                         steps, warmup)
+        ffn_ops = 2.0 * M * D * F * 3
+        out["ffn_swiglu_3b_2048x2048x11008"] = {
+            "us_per_call": ms * 1e3, "tpops": ffn_ops / ms / 1e9,
+            "frac_of_int8_peak": ffn_ops / ms / 1e9 / (2.0 * peaks["bf16"]), "bound": "tensor",
+            "torch_bf16_us_per_call": bms * 1e3, "launches_per_call": 4}
+    if want("bp8"):
+        # bposit8 operands (uniform codes) rotated over > 3x L2
+        M = N = K = 4096
+        nsets = max(2, math.ceil(3 * L2_BYTES / (M * K + N * K)))
+        A8 = [torch.randint(0, 256, (M, K), device="cuda", generator=g, dtype=torch.int32)
+              .to(torch.uint8) for _ in range(nsets)]
+        B8 = [torch.randint(0, 256, (N, K), device="cuda", generator=g, dtype=torch.int32)
+              .to(torch.uint8) for _ in range(nsets)]
+        it[0] = 0
+
+        def bp8():
+            i = it[0] % nsets
+            it[0] += 1
+            ops.gemm_bposit8(A8[i], B8[i])
+        ms = _events_ms(bp8, steps, warmup)
+        out["bposit8_gemm_4096"] = {
+            "us_per_call": ms * 1e3, "tpops": 2.0 * M * N * K / ms / 1e9,
+            "frac_of_int8_peak": 2.0 * M * N * K / ms / 1e9 / (2.0 * peaks["bf16"]),
+            "bound": "tensor", "launches_per_call": 3,
+            "steps": "decode A, decode B (bposit8 -> int8 x 2^6), GEMM -> bposit32 of acc / 2^12"}
+        del A8, B8
     return out
+
+
+def kernel_table(steps, warmup, peaks):
+    """Device time and achieved HBM bandwidth of the element-wise and
+    quantisation kernels of the path, one call each on inputs larger than
+    L2 (so every call reads its input from HBM).  Bytes are the compulsory
+    ones: each input read once, each output written once."""
+    import torch
+
+    from mosyne_bposit import ops
+    hbm = peaks["hbm"]
+    g = torch.Generator(device="cuda").manual_seed(7)
+    res = {}
+
+    def row(name, fn, nbytes, launches=1, **extra):
+        ms = _events_ms(fn, steps, warmup)
+        res[name] = {"us_per_call": ms * 1e3, "bytes_per_call": nbytes,
+                     "achieved_gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / hbm,
+                     "launches_per_call": launches, **extra}
+
+    M, K = 8192, 4096                                    # activations, 128 MiB fp32
+    x = torch.randn(M, K, device="cuda", generator=g)
+    row("quant_per_token_rowmajor_8192x4096_f32", lambda: ops.quantize_per_token(x),
+        M * K * 4 + M * K + M * 4)
+    xb = x.bfloat16()
+    row("quant_per_token_rowmajor_8192x4096_bf16", lambda: ops.quantize_per_token(xb),
+        M * K * 2 + M * K + M * 4)
+    xc = x.t().contiguous()                              # column-major [M, K] storage
+    row("quant_per_token_colmajor_8192x4096_f32",
+        lambda: ops.quantize_per_token(xc, col_major=True), M * K * 4 + M * K + M * 4,
+        launches=2)
+    del xc
+    row("quant_per_tensor_8192x4096_f32", lambda: ops.quantize_per_tensor(x),
+        M * K * 4 + M * K + 4, launches=2,
+        note="absmax pass, then the quantise pass (which also writes the scale): "
+             "the input is read twice")
+    del x, xb
+    N, Kw = 14336, 4096                                  # FFN gate weight, 224 MiB fp32
+    w = torch.randn(N, Kw, device="cuda", generator=g) * 0.02
+    row("quant_per_channel_14336x4096_f32", lambda: ops.quantize_per_channel(w),
+        N * Kw * 4 + N * Kw + N * 4)
+    del w
+    n = 1 << 25                                          # 32 M elements
+    i32 = torch.randint(-(1 << 31), 1 << 31, (n,), device="cuda", generator=g,
+                        dtype=torch.int64).to(torch.int32)
+    row("int32_to_bp32_2^25", lambda: ops.int32_to_bp32(i32), 8 * n)
+    acc = i32[: 8192 * 4096].view(4096, 8192).t()        # logical [8192, 4096], column-major
+    xs = torch.rand(8192, device="cuda", generator=g) + 0.5
+    wsc = torch.rand(4096, device="cuda", generator=g) + 0.5
+    row("epilogue_i32_8192x4096_bp32_f32",
+        lambda: ops.epilogue_i32(acc, bp32=True, y_dtype=torch.float32, x_scale=xs, w_scale=wsc),
+        8192 * 4096 * 12 + 8192 * 4 + 4096 * 4)
+    del i32, acc
+    f = torch.randn(n, device="cuda", generator=g)
+    row("float_to_bp16_rtne_2^25_f32", lambda: ops.float_to_bposit(f, 16, rtne=True), 6 * n)
+    del f
+    codes = torch.randint(-(1 << 15), 1 << 15, (n,), device="cuda", generator=g,
+                          dtype=torch.int32).to(torch.int16)
+    codes2 = torch.randint(-(1 << 15), 1 << 15, (n,), device="cuda", generator=g,
+                           dtype=torch.int32).to(torch.int16)
+    for op in ("add", "mul", "recip", "sqrt", "log2", "exp2"):
+        if op in ("add", "mul"):
+            row(f"bposit16_{op}_2^25", lambda op=op: ops.bposit16_op(op, codes, codes2), 6 * n)
+        else:
+            row(f"bposit16_{op}_2^25", lambda op=op: ops.bposit16_op(op, codes), 4 * n)
+    del codes2
+    nq = 1 << 22                                         # 4 M quires, 128 MiB
+    q = ops.bp16_to_quire(codes[:nq])
+    row("bp16_to_quire_2^22", lambda: ops.bp16_to_quire(codes[:nq]), 34 * nq)
+    row("quire_to_bp32_2^22", lambda: ops.quire_to_bposit(q, 32), 36 * nq)
+    row("quire_to_bp16_rtne_2^22", lambda: ops.quire_to_bposit(q, 16, rtne=True), 34 * nq)
+    del q, codes
+    b8 = torch.randint(0, 256, (1 << 27,), device="cuda", generator=g,
+                       dtype=torch.int32).to(torch.uint8)
+    row("bposit8_to_int8_2^27", lambda: ops.bposit8_to_int8(b8), 2 << 27)
+    del b8
+    return res
 
 
 def ksplit_workload(dist, ws, steps, warmup):
@@ -533,6 +649,7 @@ def run_ours(args):
         line["workloads"]["ksplit_4096x4096xK"] = ksplit
     if ws == 1:
         line["workloads"].update(extra_workloads(args.steps, args.warmup, peaks))
+        line["kernels"] = kernel_table(args.steps, args.warmup, peaks)
         line["cpu_baseline"] = cpu_baseline(M, N, K)
     print(json.dumps(line), flush=True)
     if dist is not None:
@@ -555,6 +672,25 @@ def run_only_gemm(args):
                       "device_error": rc}), flush=True)
 
 
+def run_tables(args):
+    """--workloads / --kernels: only the selected secondary rows (for
+    profilers); prints one JSON line."""
+    import torch
+
+    from mosyne_bposit import _api
+    torch.cuda.set_device(0)
+    _api.load_library(init=True)
+    peaks = _peaks()
+    line = {}
+    if args.workloads:
+        sel = None if args.workloads == "all" else set(args.workloads.split(","))
+        line["workloads"] = extra_workloads(args.steps, args.warmup, peaks, sel)
+    if args.kernels:
+        line["kernels"] = kernel_table(args.steps, args.warmup, peaks)
+    line["device_error"] = _api.last_error()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -566,11 +702,17 @@ def main():
     ap.add_argument("--gemm-flags", type=lambda v: int(v, 0), default=0,
                     help="flags word passed to mosyne_bposit_gemm_i8 with --only-gemm "
                          "(e.g. 0x100000 * (1 + cut) pins the last-wave cut)")
+    ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,bp8|all",
+                    help="run only these secondary workloads and print them (for profilers)")
+    ap.add_argument("--kernels", action="store_true",
+                    help="run only the element-wise / quantiser kernel table (for profilers)")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and not (args.workloads or args.kernels):
         args.warmup = 3
     if args.only_gemm:
         run_only_gemm(args)
+    elif args.workloads or args.kernels:
+        run_tables(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

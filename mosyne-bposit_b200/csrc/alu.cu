@@ -19,12 +19,13 @@ constexpr uint32_t NAR = 0x8000u;
 constexpr uint32_t ONE = 0x4000u;
 constexpr int TAB_BYTES = 65536 * 2;
 
-// add via the quire (bposit16_encode.cuh:472-483; bposit16_reference.py:758-772)
+// add = truncating encode of the exact quire sum (bposit16_encode.cuh:472-483;
+// bposit16_reference.py:758-772), the sum taken in an int64 (bp::sum16_trunc)
 __device__ __forceinline__ uint32_t add16(uint32_t a, uint32_t b) {
   if (a == NAR || b == NAR) return NAR;
   if (a == 0) return b;
   if (b == 0) return a;
-  return bp::from_quire<16>(bp::q_add(bp::quire_from_bp16(a), bp::quire_from_bp16(b)), false);
+  return bp::sum16_trunc(a, b);
 }
 
 // exact product, truncated (bposit16_reference.py:507-516; zero before NaR)
@@ -49,8 +50,7 @@ __device__ __forceinline__ uint32_t mul16_logexp(uint32_t a, uint32_t b, const u
   if (b == ONE) return a;
   const bool rs = ((a ^ b) >> 15) & 1u;
   const uint32_t la = lg[abs16(a)], lb = lg[abs16(b)];
-  const uint32_t ls =
-      bp::from_quire<16>(bp::q_add(bp::quire_from_bp16(la), bp::quire_from_bp16(lb)), false);
+  const uint32_t ls = bp::sum16_trunc(la, lb);           // quire add of the logarithms
   const uint32_t mag = __ldg(ex + ls);
   if (mag == NAR || mag == 0) return mag;
   return rs ? ((0u - mag) & 0xFFFFu) : mag;
@@ -70,12 +70,34 @@ __device__ __forceinline__ uint32_t apply(uint32_t a, uint32_t b, const uint16_t
 }
 
 // Element-wise kernel; STAGE copies table t0 into shared memory first.
+// Each thread keeps U independent 16-byte vectors (8 codes each) in flight.
+template <Op OP>
+__device__ __forceinline__ uint4 apply8(uint4 ra, uint4 rb, const uint16_t* tab,
+                                        const uint16_t* t1) {
+  const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
+  const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+  uint32_t wo[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = apply<OP>(wa[j] & 0xFFFFu, wb[j] & 0xFFFFu, tab, t1);
+    const uint32_t hi = apply<OP>(wa[j] >> 16, wb[j] >> 16, tab, t1);
+    wo[j] = (lo & 0xFFFFu) | (hi << 16);
+  }
+  return make_uint4(wo[0], wo[1], wo[2], wo[3]);
+}
+
+template <Op OP>
+__host__ __device__ constexpr int ew_unroll() {
+  return (OP == OP_ADD || OP == OP_MUL || OP == OP_MUL_EXACT) ? 2 : 4;
+}
+
 template <Op OP, bool STAGE>
-__global__ void __launch_bounds__(512) ew_kernel(const uint16_t* __restrict__ a,
-                                                 const uint16_t* __restrict__ b, size_t n,
-                                                 uint16_t* __restrict__ out,
-                                                 const uint16_t* __restrict__ t0,
-                                                 const uint16_t* __restrict__ t1) {
+__global__ void __launch_bounds__(1024) ew_kernel(const uint16_t* __restrict__ a,
+                                                  const uint16_t* __restrict__ b, size_t n,
+                                                  uint16_t* __restrict__ out,
+                                                  const uint16_t* __restrict__ t0,
+                                                  const uint16_t* __restrict__ t1) {
+  constexpr int U = ew_unroll<OP>();
   extern __shared__ __align__(16) uint16_t s_tab[];
   const uint16_t* tab = t0;
   if (STAGE) {
@@ -93,20 +115,26 @@ __global__ void __launch_bounds__(512) ew_kernel(const uint16_t* __restrict__ a,
   size_t done = 0;
   if (vec) {
     const size_t nv = n / 8;
-    for (size_t i = tid; i < nv; i += stride) {
-      const uint4 ra = __ldg(reinterpret_cast<const uint4*>(a) + i);
-      uint4 rb = make_uint4(0, 0, 0, 0);
-      if (b) rb = __ldg(reinterpret_cast<const uint4*>(b) + i);
-      const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
-      const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
-      uint32_t wo[4];
+    const uint4* av = reinterpret_cast<const uint4*>(a);
+    const uint4* bv = reinterpret_cast<const uint4*>(b);
+    uint4* ov = reinterpret_cast<uint4*>(out);
+    for (size_t i0 = tid; i0 < nv; i0 += U * stride) {
+      uint4 ra[U], rb[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = apply<OP>(wa[j] & 0xFFFFu, wb[j] & 0xFFFFu, tab, t1);
-        const uint32_t hi = apply<OP>(wa[j] >> 16, wb[j] >> 16, tab, t1);
-        wo[j] = (lo & 0xFFFFu) | (hi << 16);
+      for (int u = 0; u < U; ++u) {
+        const size_t i = i0 + u * stride;
+        ra[u] = make_uint4(0, 0, 0, 0);
+        rb[u] = make_uint4(0, 0, 0, 0);
+        if (i < nv) {
+          ra[u] = __ldcs(av + i);
+          if (b) rb[u] = __ldcs(bv + i);
+        }
       }
-      reinterpret_cast<uint4*>(out)[i] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const size_t i = i0 + u * stride;
+        if (i < nv) __stcs(ov + i, apply8<OP>(ra[u], rb[u], tab, t1));
+      }
     }
     done = nv * 8;
   }
@@ -122,6 +150,7 @@ int launch_ew(DeviceContext* ctx, const uint16_t* a, const uint16_t* b, size_t n
   const bool table_op = (OP == OP_LUT || OP == OP_MUL);
   const bool stage = table_op && n >= (size_t)ctx->num_sms * 16384;
   if (stage) {
+    // one CTA of 1024 threads per SM holding the 128 KiB table
     static bool attr[kMaxDevices] = {};
     if (!attr[ctx->device]) {
       if (cudaFuncSetAttribute(ew_kernel<OP, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -129,13 +158,11 @@ int launch_ew(DeviceContext* ctx, const uint16_t* a, const uint16_t* b, size_t n
         return RC_LAUNCH;
       attr[ctx->device] = true;
     }
-    ew_kernel<OP, true><<<ctx->num_sms, 512, TAB_BYTES, st>>>(a, b, n, out, t0, t1);
+    ew_kernel<OP, true><<<ctx->num_sms, 1024, TAB_BYTES, st>>>(a, b, n, out, t0, t1);
   } else {
-    size_t blocks = (n + 8 * 512 - 1) / (8 * 512);
-    const size_t cap = (size_t)ctx->num_sms * 4;
-    if (blocks > cap) blocks = cap;
-    if (blocks == 0) blocks = 1;
-    ew_kernel<OP, false><<<(unsigned)blocks, 512, 0, st>>>(a, b, n, out, t0, t1);
+    const unsigned blocks = stream_grid((const void*)ew_kernel<OP, false>, 256, 0, ctx->num_sms,
+                                        (n + 8 * 256 - 1) / (8 * 256));
+    ew_kernel<OP, false><<<blocks, 256, 0, st>>>(a, b, n, out, t0, t1);
   }
   return launch_rc();
 }

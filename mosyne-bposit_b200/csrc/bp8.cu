@@ -5,8 +5,8 @@
 // The 256-entry table travels in the kernel's parameter space; each block
 // spreads it over shared memory as 32 copies of 256 words, copy l in bank l,
 // so the 32 lanes of a warp look up 32 arbitrary codes in one conflict-free
-// wavefront.  Each thread moves 16 bytes per step (one 128-bit load and
-// store); a head/tail pass handles unaligned ends.
+// wavefront.  Each thread keeps four 16-byte loads in flight and stores
+// 16 bytes per vector; a head/tail pass handles unaligned ends.
 #include <cstdint>
 
 #include "bp8.cuh"
@@ -52,14 +52,26 @@ __global__ void __launch_bounds__(kBp8Threads) bp8_to_i8_kernel(
   for (size_t i = tail0 + tid; i < n; i += stride) out[i] = tab.v[in[i]];
   const uint4* src = reinterpret_cast<const uint4*>(in + head);
   uint4* dst = reinterpret_cast<uint4*>(out + head);
-  for (size_t i = tid; i < nvec; i += stride) {
-    const uint4 w = __ldcs(src + i);
-    uint4 r;
-    r.x = decode4(lut, lane4, w.x);
-    r.y = decode4(lut, lane4, w.y);
-    r.z = decode4(lut, lane4, w.z);
-    r.w = decode4(lut, lane4, w.w);
-    __stcs(dst + i, r);
+  constexpr int U = 4;                       // independent 16-byte loads in flight
+  for (size_t i0 = tid; i0 < nvec; i0 += U * stride) {
+    uint4 w[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nvec) w[u] = __ldcs(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nvec) {
+        uint4 r;
+        r.x = decode4(lut, lane4, w[u].x);
+        r.y = decode4(lut, lane4, w[u].y);
+        r.z = decode4(lut, lane4, w[u].z);
+        r.w = decode4(lut, lane4, w[u].w);
+        __stcs(dst + i, r);
+      }
+    }
   }
 }
 
@@ -92,12 +104,10 @@ int bp8_to_i8_run(const uint8_t* in, size_t n, int8_t* out, int num_sms, cudaStr
     attr_done[dev] = true;
   }
   const size_t work = nvec ? nvec : n;
-  size_t blocks = (work + kBp8Threads - 1) / kBp8Threads;
-  const size_t cap = (size_t)num_sms * 4;   // 4 x 32 KiB of tables per SM
-  if (blocks > cap) blocks = cap;
-  if (blocks == 0) blocks = 1;
-  bp8_to_i8_kernel<<<(unsigned)blocks, kBp8Threads, kBp8SmemBytes, st>>>(g_bp8_table, in, out, n,
-                                                                        head, nvec);
+  const unsigned blocks = stream_grid((const void*)bp8_to_i8_kernel, kBp8Threads, kBp8SmemBytes,
+                                      num_sms, (work + kBp8Threads - 1) / kBp8Threads);
+  bp8_to_i8_kernel<<<blocks, kBp8Threads, kBp8SmemBytes, st>>>(g_bp8_table, in, out, n, head,
+                                                              nvec);
   return launch_rc();
 }
 

@@ -14,6 +14,7 @@
 // four little-endian u64 words, 96 fraction bits.
 #pragma once
 #include <cstdint>
+#include <cstring>
 
 #if defined(__CUDACC__)
 #define BP_HD __host__ __device__ __forceinline__
@@ -69,6 +70,29 @@ BP_HD uint32_t encode_field(int scale, uint64_t frac64, bool sticky, bool rtne) 
     const bool rbit = (rest >> 63) != 0;
     const bool st = sticky || ((rest << 1) != 0);
     if (rbit && (st || (f & 1u)) && field < FMASK) field += 1u;
+  }
+  return field;
+}
+
+// encode_field for a fraction that fits 32 bits (MSB-aligned, nothing
+// beyond them): the same field in 32-bit arithmetic, for single-precision
+// inputs (the kept fraction is at most 26 bits, so every shift is < 32).
+template <int NBITS>
+BP_HD uint32_t encode_field32(int scale, uint32_t frac32, bool rtne) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  if (scale > kScaleLimit) return FMASK;
+  if (scale < -kScaleLimit) return 1u;
+  const int k = scale >> 3;
+  const int e = scale & 7;
+  const int rlen = k >= 0 ? k + 2 : 1 - k;
+  const uint32_t regime = k >= 0 ? ((2u << k) - 1u) << (N1 - (k + 1)) : 1u << (N1 - rlen);
+  const int fw = N1 - rlen - 3;
+  const uint32_t f = frac32 >> (32 - fw);
+  uint32_t field = regime | ((uint32_t)e << fw) | f;
+  if (rtne) {
+    const uint32_t rest = frac32 << fw;
+    if ((rest >> 31) && (((rest << 1) != 0u) || (f & 1u)) && field < FMASK) field += 1u;
   }
   return field;
 }
@@ -407,6 +431,43 @@ BP_HD quire256 quire_from_bp16(uint32_t p) {
   return d.neg ? q_neg(q) : q;
 }
 
+// from_quire<16>(quire_from_bp16(a) + quire_from_bp16(b), truncate) without
+// the 256-bit quire.  Each operand is m * 2^x (m < 2^13; zero and NaR count
+// as 0, and bits below 2^-96 are dropped as the per-value quire conversion
+// drops them).  Aligned at the smaller exponent the exact sum fits an int64
+// while the exponents differ by at most 48.  Beyond that the smaller operand
+// is below 2^(x_hi - 35), far under the last kept place of any result near
+// the larger one (at least 2^(x_hi - 2)), so the truncated encoding depends
+// only on its sign; it is moved up to the gap of 48, which keeps the sign and
+// stays under that bound.
+BP_HD uint32_t sum16_trunc(uint32_t a, uint32_t b) {
+  const Dec16 da = decode16(a), db = decode16(b);
+  int64_t ma = (da.zero || da.nar) ? 0 : (int64_t)da.mant;
+  int64_t mb = (db.zero || db.nar) ? 0 : (int64_t)db.mant;
+  int xa = da.exp2, xb = db.exp2;
+  if (xa < -kQuireFracBits) {
+    const int s = -kQuireFracBits - xa;
+    ma = s >= 32 ? 0 : (ma >> s);
+    xa = -kQuireFracBits;
+  }
+  if (xb < -kQuireFracBits) {
+    const int s = -kQuireFracBits - xb;
+    mb = s >= 32 ? 0 : (mb >> s);
+    xb = -kQuireFracBits;
+  }
+  if (ma == 0) xa = xb;                    // a zero operand opens no gap
+  if (mb == 0) xb = xa;
+  if (da.neg) ma = -ma;
+  if (db.neg) mb = -mb;
+  const bool a_hi = xa >= xb;
+  const int xh = a_hi ? xa : xb;
+  int xl = a_hi ? xb : xa;
+  const int64_t mh = a_hi ? ma : mb, ml = a_hi ? mb : ma;
+  if (xh - xl > 48) xl = xh - 48;
+  const int64_t I = (int64_t)((uint64_t)mh << (xh - xl)) + ml;
+  return from_int64<16>(I, -xl, false);
+}
+
 // Exact binary float (value = m * 2^(e)) -> bposit<NBITS>: the exact
 // rational the float denotes (bposit16_reference.py:485-503 given a Fraction).
 template <int NBITS>
@@ -429,6 +490,95 @@ BP_HD uint32_t from_double(double x, bool rtne) {
     frac = man << 12;
   }
   return apply_sign<NBITS>(encode_field<NBITS>(scale, frac, false, rtne), neg);
+}
+
+// from_double of a single-precision value, in 32-bit integer arithmetic
+// (every float is exactly a double, so the two agree on every input).
+template <int NBITS>
+BP_HD uint32_t from_float(float x, bool rtne) {
+  uint32_t u;
+#if defined(__CUDA_ARCH__)
+  u = __float_as_uint(x);
+#else
+  std::memcpy(&u, &x, sizeof(u));
+#endif
+  const bool neg = (u >> 31) != 0;
+  const int bexp = (int)((u >> 23) & 0xFFu);
+  const uint32_t man = u & 0x7FFFFFu;
+  if (bexp == 0 && man == 0) return 0u;
+  if (bexp == 0xFF) return 1u << (NBITS - 1);             // inf/nan -> NaR
+  int scale;
+  uint32_t frac;
+  if (bexp == 0) {                                          // subnormal
+    const int lz = clz32(man);
+    scale = -149 + (31 - lz);
+    frac = (man << lz) << 1;
+  } else {
+    scale = bexp - 127;
+    frac = man << 9;
+  }
+  return apply_sign<NBITS>(encode_field32<NBITS>(scale, frac, rtne), neg);
+}
+
+// Table-driven form of from_float for streaming kernels.  For a normal
+// float the regime, exponent and fraction width depend only on the biased
+// exponent, so a 256-entry table (entry bexp) holds prefix = regime | e << fw
+// and the shifts 32 - fw (fraction) and fw (rounding remainder); exponents
+// outside the +-48 range (and subnormals, all below 2^-126) hold the
+// saturated field with both shifts 32, which clears fraction and remainder.
+// Zero and inf/nan are selected separately.
+struct F32Entry {
+  uint32_t prefix;
+  uint32_t sh;     // shift of the fraction | shift of the remainder << 8
+};
+
+template <int NBITS>
+BP_HD F32Entry f32_table_entry(int bexp) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  const int scale = bexp - 127;
+  if (bexp == 0 || scale < -kScaleLimit) return F32Entry{1u, 32u | (32u << 8)};
+  if (scale > kScaleLimit) return F32Entry{FMASK, 32u | (32u << 8)};
+  const int k = scale >> 3, e = scale & 7;
+  const int rlen = k >= 0 ? k + 2 : 1 - k;
+  const uint32_t regime = k >= 0 ? ((2u << k) - 1u) << (N1 - (k + 1)) : 1u << (N1 - rlen);
+  const int fw = N1 - rlen - 3;
+  return F32Entry{regime | ((uint32_t)e << fw), (uint32_t)(32 - fw) | ((uint32_t)fw << 8)};
+}
+
+BP_HD uint32_t shr_clamped(uint32_t a, int n) {
+#if defined(__CUDA_ARCH__)
+  uint32_t r;
+  asm("shr.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(n));
+  return r;
+#else
+  return (uint32_t)n >= 32u ? 0u : a >> n;
+#endif
+}
+
+template <int NBITS, bool RTNE>
+BP_HD uint32_t from_float_tab(float xf, const F32Entry* tab) {
+  constexpr int N1 = NBITS - 1;
+  constexpr uint32_t FMASK = (1u << N1) - 1u;
+  constexpr uint32_t NMASK = NBITS == 32 ? 0xFFFFFFFFu : ((1u << NBITS) - 1u);
+  uint32_t u;
+#if defined(__CUDA_ARCH__)
+  u = __float_as_uint(xf);
+#else
+  std::memcpy(&u, &xf, sizeof(u));
+#endif
+  const uint32_t bexp = (u >> 23) & 0xFFu;
+  const F32Entry t = tab[bexp];
+  const uint32_t x = u << 9;                              // fraction, MSB-aligned
+  uint32_t field = t.prefix | shr_clamped(x, (int)(t.sh & 0xFFu));
+  if (RTNE) {
+    const uint32_t rest = shl_clamped(x, (int)(t.sh >> 8));
+    field += (rest >> 31) & (uint32_t)(((rest << 1) != 0u) | (field & 1u)) & (uint32_t)(field != FMASK);
+  }
+  const uint32_t m = (uint32_t)((int32_t)u >> 31);
+  const uint32_t out = ((field ^ m) - m) & NMASK;
+  const uint32_t r = (u & 0x7FFFFFFFu) == 0u ? 0u : out;
+  return bexp == 0xFFu ? (1u << N1) : r;
 }
 
 }  // namespace bp

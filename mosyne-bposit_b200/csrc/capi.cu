@@ -112,6 +112,35 @@ int ensure_scratch(void** ptr, size_t* cur, size_t need) {
   return 0;
 }
 
+int resident_blocks(const void* kernel, int threads, size_t smem, int num_sms) {
+  struct Key {
+    const void* k;
+    int threads;
+    size_t smem;
+    int sms;
+  };
+  static std::mutex mu;
+  static Key keys[128];
+  static int vals[128];
+  static int used = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i].k == kernel && keys[i].threads == threads && keys[i].smem == smem &&
+        keys[i].sms == num_sms)
+      return vals[i];
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int v = per_sm * num_sms;
+  if (used < 128) {
+    keys[used] = Key{kernel, threads, smem, num_sms};
+    vals[used] = v;
+    ++used;
+  }
+  return v;
+}
+
 namespace {
 
 // Streams and events of the pipelined host-buffer GEMM, per device, made on

@@ -56,6 +56,20 @@ DeviceContext* ctx_current();       // context of the current device, or nullptr
 DeviceContext* ctx_get_or_init();   // initialise lazily (for the new entry points)
 int ensure_scratch(void** ptr, size_t* cur, size_t need);
 
+// Blocks of `kernel` (with `threads` threads and `smem` dynamic shared bytes)
+// that are resident at once on the current device: num_sms times the
+// occupancy limit, cached per kernel.  Grid-stride kernels launch at most
+// this many, so every block runs in the first and only wave.
+int resident_blocks(const void* kernel, int threads, size_t smem, int num_sms);
+
+// min(work, resident_blocks(...)), at least 1.
+inline unsigned stream_grid(const void* kernel, int threads, size_t smem, int num_sms,
+                            size_t work_blocks) {
+  const size_t cap = (size_t)resident_blocks(kernel, threads, smem, num_sms);
+  size_t b = work_blocks < cap ? work_blocks : cap;
+  return (unsigned)(b == 0 ? 1 : b);
+}
+
 // error codes (reference: libmosyne_bposit.cu:95-143, 322-348)
 constexpr int RC_OK = 0;
 constexpr int RC_LAUNCH = -1;

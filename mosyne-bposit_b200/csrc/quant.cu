@@ -41,10 +41,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
                                                          int8_t* __restrict__ q,
                                                          float* __restrict__ scale,
                                                          const uint32_t* __restrict__ given_amax,
-                                                         int amax_stride) {
+                                                         int amax_stride, int reverse) {
   constexpr int V = Vec<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
+  const int row = (reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x) * 8 + warp;
   if (row >= R) return;
   const T* xr = x + (size_t)row * C;
   int8_t* qr = q + (size_t)row * C;
@@ -90,10 +90,11 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) quant_row_block_kernel(
     const T* __restrict__ x, int C, int8_t* __restrict__ q, float* __restrict__ scale,
-    const uint32_t* __restrict__ given_amax, int amax_stride, float* __restrict__ scalar_scale) {
+    const uint32_t* __restrict__ given_amax, int amax_stride, float* __restrict__ scalar_scale,
+    int reverse) {
   constexpr int V = Vec<T>::N;
   __shared__ float red[8];
-  const int row = blockIdx.x;
+  const int row = reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
   const T* xr = x + (size_t)row * C;
   int8_t* qr = q + (size_t)row * C;
   float m = 0.f;
@@ -133,6 +134,54 @@ __global__ void __launch_bounds__(256) quant_row_block_kernel(
     }
   } else {
     for (int c = threadIdx.x; c < C; c += 256) qr[c] = quantize1(to_f32<T>(xr[c]), s);
+  }
+}
+
+// One CTA per row with the whole row held in registers between the max and
+// the quantise step, so the row is read from HBM once (a two-pass kernel
+// re-reads it, and with thousands of rows in flight the second read misses
+// L2).  NV 16-byte vectors per thread cover rows of up to 256 * NV * V
+// elements; each of the NV loads is one 4 KiB coalesced block read.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) quant_row_reg_kernel(const T* __restrict__ x, int C,
+                                                            int8_t* __restrict__ q,
+                                                            float* __restrict__ scale) {
+  constexpr int V = Vec<T>::N;
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const T* xr = x + (size_t)row * C;
+  int8_t* qr = q + (size_t)row * C;
+  uint4 raw[NV];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 256 + (int)threadIdx.x) * V;
+    raw[j] = c < C ? __ldcs(reinterpret_cast<const uint4*>(xr + c)) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const T* v = reinterpret_cast<const T*>(&raw[j]);
+#pragma unroll
+    for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32<T>(v[i])));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
+            fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+  const float s = quant_scale_from_max(m);
+  if (threadIdx.x == 0 && scale) scale[row] = s;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 256 + (int)threadIdx.x) * V;
+    if (c < C) {
+      const T* v = reinterpret_cast<const T*>(&raw[j]);
+      int8_t o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = quantize1(to_f32<T>(v[i]), s);
+      if (V == 4) __stcs(reinterpret_cast<unsigned int*>(qr + c), *reinterpret_cast<unsigned int*>(o));
+      else __stcs(reinterpret_cast<uint2*>(qr + c), *reinterpret_cast<uint2*>(o));
+    }
   }
 }
 
@@ -203,6 +252,131 @@ __global__ void __launch_bounds__(256) colmajor_quant_kernel(const T* __restrict
   }
 }
 
+// Four consecutive elements of T as floats (16 bytes of fp32, 8 of bf16/fp16).
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+  return __ldcs(reinterpret_cast<const float4*>(p));
+}
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p) {
+  const uint2 r = __ldcs(reinterpret_cast<const uint2*>(p));
+  const T* v = reinterpret_cast<const T*>(&r);
+  return make_float4(to_f32<T>(v[0]), to_f32<T>(v[1]), to_f32<T>(v[2]), to_f32<T>(v[3]));
+}
+
+// Column-major x [M,K] with M % 4 == 0 (every column 4-element aligned):
+// each lane takes 4 consecutive rows m, a warp 128 rows of one column k; the
+// 8 warps of a block walk the block's K range 8 columns apart with four
+// loads in flight each; per-row maxima go through shared memory to one
+// atomicMax per row and block.
+template <typename T>
+__global__ void __launch_bounds__(256) colmajor_rowmax_vec_kernel(const T* __restrict__ x, int M,
+                                                                  int K, int k_chunk,
+                                                                  uint32_t* __restrict__ amax) {
+  __shared__ float red[8][128];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = blockIdx.x * 128 + lane * 4;
+  const int k_begin = blockIdx.y * k_chunk;
+  const int k_end = min(K, k_begin + k_chunk);
+  float4 mx = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (m < M) {
+    for (int k = k_begin + warp; k < k_end; k += 32) {
+      float4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int kk = k + 8 * u;
+        r[u] = kk < k_end ? load4<T>(x + (size_t)kk * M + m) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mx.x = fmaxf(mx.x, fabsf(r[u].x));
+        mx.y = fmaxf(mx.y, fabsf(r[u].y));
+        mx.z = fmaxf(mx.z, fabsf(r[u].z));
+        mx.w = fmaxf(mx.w, fabsf(r[u].w));
+      }
+    }
+  }
+  red[warp][lane * 4 + 0] = mx.x;
+  red[warp][lane * 4 + 1] = mx.y;
+  red[warp][lane * 4 + 2] = mx.z;
+  red[warp][lane * 4 + 3] = mx.w;
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    float v = red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) v = fmaxf(v, red[w][threadIdx.x]);
+    const int mo = blockIdx.x * 128 + threadIdx.x;
+    if (mo < M) atomicMax(&amax[mo], __float_as_uint(v));
+  }
+}
+
+// Column-major x [M,K] (M % 4 == 0) -> int8 [M,K] row-major, 64x64 tiles:
+// each thread loads a 4x4 block (4 rows m at 4 columns k; four loads in
+// flight), quantises it and transposes it in registers into four 32-bit
+// words of 4 consecutive k for one m; a padded shared tile of words then
+// gives each output row as 16-byte stores.  With `reverse` the tiles run
+// last to first, so the columns the max pass read last are still in L2.
+template <typename T>
+__global__ void __launch_bounds__(256) colmajor_quant_vec_kernel(const T* __restrict__ x, int M,
+                                                                 int K,
+                                                                 const uint32_t* __restrict__ amax,
+                                                                 int amax_stride,
+                                                                 int8_t* __restrict__ q,
+                                                                 float* __restrict__ scale,
+                                                                 int reverse) {
+  __shared__ uint32_t tile[64][17];
+  __shared__ float srow[64];
+  const unsigned nb = gridDim.x * gridDim.y;
+  const unsigned b = blockIdx.y * gridDim.x + blockIdx.x;
+  const unsigned rb = reverse ? nb - 1 - b : b;
+  const int m0 = (int)(rb % gridDim.x) * 64, k0 = (int)(rb / gridDim.x) * 64;
+  if (threadIdx.x < 64) {
+    const int m = m0 + threadIdx.x;
+    const float s = m < M ? quant_scale_from_max(__uint_as_float(amax[(size_t)m * amax_stride])) : 1.f;
+    srow[threadIdx.x] = s;
+    if (scale && k0 == 0 && m < M && (amax_stride || m == 0)) scale[m] = s;
+  }
+  __syncthreads();
+  const int mq = threadIdx.x & 15, kq = threadIdx.x >> 4;   // 4-row group, 4-column group
+  const int m = m0 + 4 * mq, kb = k0 + 4 * kq;
+  float4 r[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int k = kb + u;
+    r[u] = (m < M && k < K) ? load4<T>(x + (size_t)k * M + m) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float s0 = srow[4 * mq], s1 = srow[4 * mq + 1], s2 = srow[4 * mq + 2], s3 = srow[4 * mq + 3];
+  uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;                  // row m+i, columns kb..kb+3
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    w0 |= (uint32_t)(uint8_t)quantize1(r[u].x, s0) << (8 * u);
+    w1 |= (uint32_t)(uint8_t)quantize1(r[u].y, s1) << (8 * u);
+    w2 |= (uint32_t)(uint8_t)quantize1(r[u].z, s2) << (8 * u);
+    w3 |= (uint32_t)(uint8_t)quantize1(r[u].w, s3) << (8 * u);
+  }
+  tile[4 * mq + 0][kq] = w0;
+  tile[4 * mq + 1][kq] = w1;
+  tile[4 * mq + 2][kq] = w2;
+  tile[4 * mq + 3][kq] = w3;
+  __syncthreads();
+  // 64 rows x 4 chunks of 16 bytes
+  const int rr = threadIdx.x >> 2, c = threadIdx.x & 3;
+  const int mo = m0 + rr, ko = k0 + 16 * c;
+  if (mo < M && ko < K) {
+    int8_t* dst = q + (size_t)mo * K + ko;
+    const uint4 v = make_uint4(tile[rr][4 * c], tile[rr][4 * c + 1], tile[rr][4 * c + 2],
+                               tile[rr][4 * c + 3]);
+    if (((K & 15) == 0) && (ko + 16 <= K)) {
+      *reinterpret_cast<uint4*>(dst) = v;
+    } else {
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(&v);
+      for (int i = 0; i < 16 && ko + i < K; ++i) dst[i] = (int8_t)vb[i];
+    }
+  }
+}
+
 template <typename T, int V>
 __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, size_t n,
                                                      uint32_t* __restrict__ amax) {
@@ -212,11 +386,21 @@ __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, si
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   if (V > 1) {
     const size_t nv = n / V;
-    for (size_t i = tid; i < nv; i += stride) {
-      const uint4 raw = reinterpret_cast<const uint4*>(x)[i];
-      const T* v = reinterpret_cast<const T*>(&raw);
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    constexpr int U = 4;                     // independent 16-byte loads in flight
+    for (size_t i0 = tid; i0 < nv; i0 += U * stride) {
+      uint4 raw[U];
 #pragma unroll
-      for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32<T>(v[j])));
+      for (int u = 0; u < U; ++u) {
+        const size_t i = i0 + u * stride;
+        raw[u] = i < nv ? __ldcs(xv + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T* v = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32<T>(v[j])));
+      }
     }
     for (size_t i = nv * V + tid; i < n; i += stride) m = fmaxf(m, fabsf(to_f32<T>(x[i])));
   } else {
@@ -255,28 +439,89 @@ __global__ void __launch_bounds__(256) rowmax_rows_kernel(const T* __restrict__ 
 // (a warp per row would leave most SMs idle).
 constexpr int kBlockPerRowMax = 2048;
 
+template <typename T, int NV>
+void launch_row_reg(const void* x, int R, int C, int8_t* q, float* scale, cudaStream_t st) {
+  quant_row_reg_kernel<T, NV><<<(unsigned)R, 256, 0, st>>>(static_cast<const T*>(x), C, q, scale);
+}
+
+// `reverse` walks the rows last to first: after a pass that streamed the
+// whole tensor (the per-tensor max), the rows it read last are still in L2.
 template <typename T>
 int quant_rows_t(const void* x, int R, int C, int8_t* q, float* scale, const uint32_t* amax,
-                 cudaStream_t st, int amax_stride = 0, float* scalar_scale = nullptr) {
+                 cudaStream_t st, int amax_stride = 0, float* scalar_scale = nullptr,
+                 int reverse = 0) {
   constexpr int V = Vec<T>::N;
   const bool vec = (C % V == 0) && aligned16<T>(x) && ((reinterpret_cast<uintptr_t>(q) % V) == 0);
+  if (!amax && !scalar_scale && vec && C <= 256 * V * 16) {
+    const int nv = (C + 256 * V - 1) / (256 * V);     // 16-byte vectors per thread
+    if (nv <= 1) launch_row_reg<T, 1>(x, R, C, q, scale, st);
+    else if (nv <= 2) launch_row_reg<T, 2>(x, R, C, q, scale, st);
+    else if (nv <= 4) launch_row_reg<T, 4>(x, R, C, q, scale, st);
+    else if (nv <= 8) launch_row_reg<T, 8>(x, R, C, q, scale, st);
+    else launch_row_reg<T, 16>(x, R, C, q, scale, st);
+    return launch_rc();
+  }
   if (R <= kBlockPerRowMax || scalar_scale) {
     if (vec)
       quant_row_block_kernel<T, true><<<(unsigned)R, 256, 0, st>>>(
-          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale);
+          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale, reverse);
     else
       quant_row_block_kernel<T, false><<<(unsigned)R, 256, 0, st>>>(
-          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale);
+          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale, reverse);
     return launch_rc();
   }
+  // warps per row; a partial last block only when R % 8 != 0, so reversing
+  // whole blocks still covers every row once
   const unsigned blocks = (unsigned)((R + 7) / 8);
   if (vec)
     quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
-                                                       amax_stride);
+                                                       amax_stride, reverse);
   else
     quant_rows_kernel<T, false><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
-                                                        amax_stride);
+                                                        amax_stride, reverse);
   return launch_rc();
+}
+
+// Column-major max pass + quantise pass; the vector kernels when every
+// column starts 4-element aligned.
+template <typename T>
+bool colmajor_vec_ok(const void* x, int M) {
+  return (M % 4) == 0 && (reinterpret_cast<uintptr_t>(x) % (4 * sizeof(T))) == 0;
+}
+
+template <typename T>
+void colmajor_rowmax_launch(const void* x, int M, int K, uint32_t* amax, int num_sms,
+                            cudaStream_t st) {
+  const T* xt = static_cast<const T*>(x);
+  if (colmajor_vec_ok<T>(x, M)) {
+    // enough K slices that every SM holds its full complement of blocks
+    const int gm = (M + 127) / 128;
+    const int target = resident_blocks((const void*)colmajor_rowmax_vec_kernel<T>, 256, 0, num_sms);
+    int splits = (target + gm - 1) / gm;
+    splits = max(1, min(splits, (K + 31) / 32));
+    const int k_chunk = (K + splits - 1) / splits;
+    colmajor_rowmax_vec_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
+        xt, M, K, k_chunk, amax);
+    return;
+  }
+  const int gm = (M + 63) / 64;
+  int splits = (2 * num_sms + gm - 1) / gm;
+  splits = max(1, min(splits, (K + 63) / 64));
+  const int k_chunk = (K + splits - 1) / splits;
+  colmajor_rowmax_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
+      xt, M, K, k_chunk, amax);
+}
+
+template <typename T>
+void colmajor_quant_launch(const void* x, int M, int K, const uint32_t* amax, int amax_stride,
+                           int8_t* q, float* scale, int reverse, cudaStream_t st) {
+  const T* xt = static_cast<const T*>(x);
+  const dim3 grid((M + 63) / 64, (K + 63) / 64);
+  if (colmajor_vec_ok<T>(x, M))
+    colmajor_quant_vec_kernel<T><<<grid, 256, 0, st>>>(xt, M, K, amax, amax_stride, q, scale,
+                                                       reverse);
+  else
+    colmajor_quant_kernel<T><<<grid, 256, 0, st>>>(xt, M, K, amax, amax_stride, q, scale);
 }
 
 template <typename T>
@@ -286,14 +531,8 @@ int colmajor_per_token_t(DeviceContext* ctx, const void* x, int M, int K, int8_t
                      (size_t)M * sizeof(uint32_t)))
     return RC_ALLOC;
   cudaMemsetAsync(ctx->amax, 0, (size_t)M * sizeof(uint32_t), st);
-  const int gm = (M + 63) / 64;
-  int splits = (2 * ctx->num_sms + gm - 1) / gm;
-  splits = max(1, min(splits, (K + 63) / 64));
-  const int k_chunk = (K + splits - 1) / splits;
-  colmajor_rowmax_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
-      static_cast<const T*>(x), M, K, k_chunk, ctx->amax);
-  colmajor_quant_kernel<T><<<dim3(gm, (K + 63) / 64), 256, 0, st>>>(static_cast<const T*>(x), M, K,
-                                                                    ctx->amax, 1, q, scale);
+  colmajor_rowmax_launch<T>(x, M, K, ctx->amax, ctx->num_sms, st);
+  colmajor_quant_launch<T>(x, M, K, ctx->amax, 1, q, scale, /*reverse=*/1, st);
   return launch_rc();
 }
 
@@ -304,20 +543,19 @@ int per_tensor_t(DeviceContext* ctx, const void* t, int rows, int cols, int8_t* 
     return RC_ALLOC;
   cudaMemsetAsync(ctx->amax, 0, sizeof(uint32_t), st);
   const size_t n = (size_t)rows * (size_t)cols;
-  size_t nb = (n + 2047) / 2048;
-  if (nb > (size_t)ctx->num_sms * 4) nb = (size_t)ctx->num_sms * 4;
-  unsigned blocks = (unsigned)nb;
-  if (blocks == 0) blocks = 1;
+  const size_t work = (n + 2047) / 2048;
   if (aligned16<T>(t))
-    absmax_kernel<T, Vec<T>::N><<<blocks, 256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
+    absmax_kernel<T, Vec<T>::N><<<stream_grid((const void*)absmax_kernel<T, Vec<T>::N>, 256, 0,
+                                              ctx->num_sms, work), 256, 0, st>>>(
+        static_cast<const T*>(t), n, ctx->amax);
   else
-    absmax_kernel<T, 1><<<blocks, 256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
+    absmax_kernel<T, 1><<<stream_grid((const void*)absmax_kernel<T, 1>, 256, 0, ctx->num_sms, work),
+                          256, 0, st>>>(static_cast<const T*>(t), n, ctx->amax);
   int rc = launch_rc();
   if (rc) return rc;
   if (row_major)   // the quantiser's row 0 also writes the per-tensor scale
-    return quant_rows_t<T>(t, rows, cols, q, nullptr, ctx->amax, st, 0, scale);
-  colmajor_quant_kernel<T><<<dim3((rows + 63) / 64, (cols + 63) / 64), 256, 0, st>>>(
-      static_cast<const T*>(t), rows, cols, ctx->amax, 0, q, scale);
+    return quant_rows_t<T>(t, rows, cols, q, nullptr, ctx->amax, st, 0, scale, /*reverse=*/1);
+  colmajor_quant_launch<T>(t, rows, cols, ctx->amax, 0, q, scale, /*reverse=*/1, st);
   return launch_rc();
 }
 
@@ -358,15 +596,10 @@ int row_absmax(DeviceContext* ctx, int dtype, const void* x, int M, int K, float
     return launch_rc();
   }
   cudaMemsetAsync(o, 0, (size_t)M * sizeof(uint32_t), st);
-  const int gm = (M + 63) / 64;
-  int splits = (2 * ctx->num_sms + gm - 1) / gm;
-  splits = max(1, min(splits, (K + 63) / 64));
-  const int k_chunk = (K + splits - 1) / splits;
-  const dim3 grid(gm, (K + k_chunk - 1) / k_chunk);
   switch (dtype) {
-    case MOSYNE_DT_F32: colmajor_rowmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), M, K, k_chunk, o); break;
-    case MOSYNE_DT_BF16: colmajor_rowmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, k_chunk, o); break;
-    case MOSYNE_DT_F16: colmajor_rowmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), M, K, k_chunk, o); break;
+    case MOSYNE_DT_F32: colmajor_rowmax_launch<float>(x, M, K, o, ctx->num_sms, st); break;
+    case MOSYNE_DT_BF16: colmajor_rowmax_launch<__nv_bfloat16>(x, M, K, o, ctx->num_sms, st); break;
+    case MOSYNE_DT_F16: colmajor_rowmax_launch<__half>(x, M, K, o, ctx->num_sms, st); break;
     default: return RC_BAD_ARG;
   }
   return launch_rc();
@@ -377,8 +610,7 @@ int quant_given_t(const void* x, int M, int K, const float* row_max, int8_t* q, 
                   bool row_major, cudaStream_t st) {
   const uint32_t* am = reinterpret_cast<const uint32_t*>(row_max);
   if (row_major) return quant_rows_t<T>(x, M, K, q, scale, am, st, 1);
-  colmajor_quant_kernel<T><<<dim3((M + 63) / 64, (K + 63) / 64), 256, 0, st>>>(
-      static_cast<const T*>(x), M, K, am, 1, q, scale);
+  colmajor_quant_launch<T>(x, M, K, am, 1, q, scale, 0, st);
   return launch_rc();
 }
 
@@ -403,14 +635,8 @@ template <typename T>
 int colmajor_per_token_into_t(const void* x, int M, int K, int8_t* q, float* scale, uint32_t* amax,
                               int num_sms, cudaStream_t st) {
   if (cudaMemsetAsync(amax, 0, (size_t)M * sizeof(uint32_t), st) != cudaSuccess) return RC_LAUNCH;
-  const int gm = (M + 63) / 64;
-  int splits = (2 * num_sms + gm - 1) / gm;
-  splits = max(1, min(splits, (K + 63) / 64));
-  const int k_chunk = (K + splits - 1) / splits;
-  colmajor_rowmax_kernel<T><<<dim3(gm, (K + k_chunk - 1) / k_chunk), 256, 0, st>>>(
-      static_cast<const T*>(x), M, K, k_chunk, amax);
-  colmajor_quant_kernel<T><<<dim3(gm, (K + 63) / 64), 256, 0, st>>>(static_cast<const T*>(x), M, K,
-                                                                    amax, 1, q, scale);
+  colmajor_rowmax_launch<T>(x, M, K, amax, num_sms, st);
+  colmajor_quant_launch<T>(x, M, K, amax, 1, q, scale, /*reverse=*/1, st);
   return launch_rc();
 }
 

@@ -61,6 +61,41 @@ __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * 256, code_sext < 0 ? -V : V);
 }
 
+// The same accumulation with the regime read from a table: the top 8 bits
+// of the 15-bit magnitude fix the regime whenever they are not all equal
+// (run length 1..7, k = -7 .. 6), so a 256-entry table gives the shift that
+// brings the exponent to the top (18 + run length, low byte) and the
+// regime's column offset (k - kGroupLow) * 256 (upper bits).  Entries 0x00
+// and 0xFF (zero, NaR and regimes of 8 or more bits) hold 0 and take the
+// general decode.  The table sits in shared memory as 16 copies per entry,
+// copy = lane & 15, so a warp's lookups conflict at most two ways.
+constexpr int kRegimeLutCopies = 16;
+constexpr int kRegimeLutBytes = 256 * kRegimeLutCopies * 4;     // 16 KiB
+
+__device__ __forceinline__ uint32_t regime_lut_entry(uint32_t hi8) {
+  if (hi8 == 0u || hi8 == 0xFFu) return 0u;
+  const uint32_t lead = hi8 >> 7;
+  const uint32_t y = hi8 << 24;
+  const int rs = __clz(y ^ (y << 1)) + 1;                 // 1..7: the run ends inside
+  const int k = lead ? rs - 1 : -rs;
+  return (uint32_t)(18 + rs) | ((uint32_t)((k - kGroupLow) * 256) << 8);
+}
+
+__device__ __forceinline__ void group_accumulate_lut(int* g, const uint32_t* lut, uint32_t copy,
+                                                     int code_sext) {
+  const uint32_t a = (uint32_t)abs(code_sext) & 0x7FFFu;
+  const uint32_t ent = lut[((a >> 7) * kRegimeLutCopies) | copy];
+  const uint32_t sa = ent & 0xFFu;
+  if (sa == 0u) {
+    group_accumulate_bp16(g, code_sext);
+    return;
+  }
+  const uint32_t z = a << sa;
+  const uint32_t e = z >> 29;
+  const int V = (int)((((z >> 18) & 0x7FFu) | 0x800u) << e);
+  atomicAdd(g + (ent >> 8), code_sext < 0 ? -V : V);
+}
+
 __device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
 #pragma unroll 1
   for (int i = 0; i < kGroups; ++i) {
@@ -108,10 +143,15 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
   __shared__ bool is_last;
-  extern __shared__ int groups[];                         // [kGroups][256]
+  extern __shared__ int groups[];                         // [kGroups][256], then the table
   int* g = groups + threadIdx.x;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(groups + kGroups * 256);
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) g[i * 256] = 0;
+  for (int i = threadIdx.x; i < 256 * kRegimeLutCopies; i += blockDim.x)
+    lut[i] = regime_lut_entry((uint32_t)i / kRegimeLutCopies);
+  __syncthreads();
+  const uint32_t copy = threadIdx.x & (kRegimeLutCopies - 1);
   quire256 acc = bp::q_zero();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -126,8 +166,8 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
-        group_accumulate_bp16(g, (int)w[j] >> 16);
+        group_accumulate_lut(g, lut, copy, (int)(w[j] << 16) >> 16);
+        group_accumulate_lut(g, lut, copy, (int)w[j] >> 16);
       }
       if (++iters == kFoldIters) {
         acc = fold_groups(g, acc);
@@ -171,32 +211,164 @@ __global__ void fp32_atomic_sum_kernel(const float* __restrict__ x, size_t n, fl
     atomicAdd(acc, x[i]);
 }
 
-template <int NB>
-__global__ void quire_to_bp_kernel(const quire256* __restrict__ q, size_t n, void* out,
-                                   int rtne) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const quire256 v = q[i];
-    const uint32_t r = bp::from_quire<NB>(v, rtne != 0);
-    if (NB == 16)
-      static_cast<uint16_t*>(out)[i] = (uint16_t)r;
-    else
-      static_cast<uint32_t*>(out)[i] = r;
+// ---------------------------------------------------------------------------
+// Element-wise conversions.  All are HBM streams: every thread keeps several
+// independent 16-byte loads in flight (an unrolled grid stride), and memory
+// is touched in whole 32-byte sectors per warp instruction wherever the
+// element size allows.
+// ---------------------------------------------------------------------------
+constexpr int kEwUnroll = 4;
+
+// quire256 -> bposit<NB>.  Each quire is two 16-byte loads (the array is
+// 16-byte aligned: the host checks and falls back to the scalar form).
+template <int NB, bool RTNE, bool VEC>
+__global__ void __launch_bounds__(256) quire_to_bp_kernel(const quire256* __restrict__ q, size_t n,
+                                                          void* out) {
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i0 = tid; i0 < n; i0 += kEwUnroll * stride) {
+    quire256 v[kEwUnroll];
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < n) {
+        if (VEC) {
+          const ulonglong2* p = reinterpret_cast<const ulonglong2*>(q + i);
+          const ulonglong2 a = __ldcs(p), b = __ldcs(p + 1);
+          v[u] = quire256{{a.x, a.y, b.x, b.y}};
+        } else {
+          v[u] = q[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < n) {
+        const uint32_t r = bp::from_quire<NB>(v[u], RTNE);
+        if (NB == 16) static_cast<uint16_t*>(out)[i] = (uint16_t)r;
+        else static_cast<uint32_t*>(out)[i] = r;
+      }
+    }
   }
 }
 
-__global__ void bp16_to_quire_kernel(const uint16_t* __restrict__ x, size_t n,
-                                     quire256* __restrict__ out) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x)
-    out[i] = bp::quire_from_bp16(x[i]);
+// bposit16 -> quire256.  Lanes 2j and 2j+1 of a warp decode the same code
+// and store its low and high 16 bytes, so every store instruction of the
+// warp writes 512 contiguous bytes (whole sectors); an output that is not
+// 16-byte aligned takes two 8-byte stores per lane instead.
+template <bool VEC>
+__global__ void __launch_bounds__(256) bp16_to_quire_kernel(const uint16_t* __restrict__ x,
+                                                            size_t n, quire256* __restrict__ out) {
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t tid = t >> 1;                                // code index of this lane pair
+  const int half = (int)(t & 1);
+  const size_t stride = ((size_t)gridDim.x * blockDim.x) >> 1;
+  for (size_t i0 = tid; i0 < n; i0 += kEwUnroll * stride) {
+    uint32_t c[kEwUnroll];
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      c[u] = i < n ? (uint32_t)__ldcs(x + i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < n) {
+        const quire256 v = bp::quire_from_bp16(c[u]);
+        const uint64_t lo = half ? v.w[2] : v.w[0], hi = half ? v.w[3] : v.w[1];
+        if (VEC) {
+          __stcs(reinterpret_cast<ulonglong2*>(out + i) + half, make_ulonglong2(lo, hi));
+        } else {
+          uint64_t* p = reinterpret_cast<uint64_t*>(out + i) + 2 * half;
+          p[0] = lo;
+          p[1] = hi;
+        }
+      }
+    }
+  }
 }
 
+// int32 -> bposit32 of I / 2^shift for shift in [0, 31], through the
+// 33-entry table of bp::i32_table_entry (four values per 16-byte vector).
+template <bool RTNE>
+__device__ __forceinline__ uint4 enc4_i32(int4 r, const bp::I32Entry* tab) {
+  return make_uint4(bp::from_int32_tab<32, RTNE>(r.x, tab), bp::from_int32_tab<32, RTNE>(r.y, tab),
+                    bp::from_int32_tab<32, RTNE>(r.z, tab), bp::from_int32_tab<32, RTNE>(r.w, tab));
+}
+
+template <bool RTNE>
+__global__ void __launch_bounds__(256) int32_to_bp32_tab_kernel(const int32_t* __restrict__ in,
+                                                                size_t n, size_t nv, int shift,
+                                                                uint32_t* __restrict__ out) {
+  __shared__ bp::I32Entry tab[33];
+  if (threadIdx.x < 33) tab[threadIdx.x] = bp::i32_table_entry<32>(threadIdx.x, shift);
+  __syncthreads();
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const int4* iv = reinterpret_cast<const int4*>(in);
+  uint4* ov = reinterpret_cast<uint4*>(out);
+  for (size_t i0 = tid; i0 < nv; i0 += kEwUnroll * stride) {
+    int4 r[kEwUnroll];
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nv) r[u] = __ldcs(iv + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nv) __stcs(ov + i, enc4_i32<RTNE>(r[u], tab));
+    }
+  }
+  for (size_t i = nv * 4 + tid; i < n; i += stride) out[i] = bp::from_int32_tab<32, RTNE>(in[i], tab);
+}
+
+// Any other shift: the general int64 path.
 __global__ void int32_to_bp32_kernel(const int32_t* __restrict__ in, size_t n, int shift,
                                      uint32_t* __restrict__ out, int rtne) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     out[i] = bp::from_int64<32>(in[i], shift, rtne != 0);
+}
+
+// float -> bposit<NB> through the 256-entry exponent table of
+// bp::f32_table_entry (shared memory), four values per 16-byte load.
+template <int NB, bool RTNE>
+__device__ __forceinline__ void store4_bp(void* out, size_t i, float4 f, const bp::F32Entry* t) {
+  const uint32_t a = bp::from_float_tab<NB, RTNE>(f.x, t), b = bp::from_float_tab<NB, RTNE>(f.y, t);
+  const uint32_t c = bp::from_float_tab<NB, RTNE>(f.z, t), d = bp::from_float_tab<NB, RTNE>(f.w, t);
+  if (NB == 16) __stcs(reinterpret_cast<uint2*>(out) + i, make_uint2(a | (b << 16), c | (d << 16)));
+  else __stcs(reinterpret_cast<uint4*>(out) + i, make_uint4(a, b, c, d));
+}
+
+template <int NB, bool RTNE>
+__global__ void __launch_bounds__(256) float_to_bp_f32_kernel(const float* __restrict__ x, size_t n,
+                                                              size_t nv, void* out) {
+  __shared__ bp::F32Entry tab[256];
+  tab[threadIdx.x] = bp::f32_table_entry<NB>((int)threadIdx.x);   // 256 threads
+  __syncthreads();
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const float4* xv = reinterpret_cast<const float4*>(x);
+  for (size_t i0 = tid; i0 < nv; i0 += kEwUnroll * stride) {
+    float4 r[kEwUnroll];
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nv) r[u] = __ldcs(xv + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kEwUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < nv) store4_bp<NB, RTNE>(out, i, r[u], tab);
+    }
+  }
+  for (size_t i = nv * 4 + tid; i < n; i += stride) {
+    const uint32_t r = bp::from_float_tab<NB, RTNE>(x[i], tab);
+    if (NB == 16) static_cast<uint16_t*>(out)[i] = (uint16_t)r;
+    else static_cast<uint32_t*>(out)[i] = r;
+  }
 }
 
 template <typename F, int NB>
@@ -210,6 +382,8 @@ __global__ void float_to_bp_kernel(const F* __restrict__ x, size_t n, void* out,
       static_cast<uint32_t*>(out)[i] = r;
   }
 }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 unsigned grid_for(size_t n, int num_sms, int per_sm = 8) {
   size_t b = (n + 255) / 256;
@@ -225,14 +399,7 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
                        uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
                        int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
-  size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
-  size_t cap = (size_t)ctx->num_sms * 8;     // 8 blocks of 27 KiB shared memory per SM
-  if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
-  if (blocks > cap) blocks = cap;
-  if (blocks == 0) blocks = 1;
-  if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
-    return RC_ALLOC;
-  constexpr int kSumSmem = kGroups * 256 * sizeof(int);         // 27 KiB
+  constexpr int kSumSmem = kGroups * 256 * sizeof(int) + kRegimeLutBytes;   // 43 KiB
   static bool attr_done[kMaxDevices] = {};
   if (!attr_done[ctx->device]) {
     if (cudaFuncSetAttribute(quire_sum_bp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -240,6 +407,15 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
       return RC_LAUNCH;
     attr_done[ctx->device] = true;
   }
+  size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
+  // every block resident at once (shared memory bounds the blocks per SM)
+  size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel, 256, kSumSmem,
+                                       ctx->num_sms);
+  if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
+    return RC_ALLOC;
   quire_sum_bp16_kernel<<<(unsigned)blocks, 256, kSumSmem, st>>>(
       x, n, static_cast<quire256*>(ctx->partials), ctx->ticket,
       reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
@@ -257,38 +433,74 @@ int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void
                     int rtne, cudaStream_t st) {
   if (n == 0) return RC_OK;
   const auto* qq = reinterpret_cast<const quire256*>(q);
-  if (nbits == 16)
-    quire_to_bp_kernel<16><<<grid_for(n, ctx->num_sms), 256, 0, st>>>(qq, n, out, rtne);
-  else
-    quire_to_bp_kernel<32><<<grid_for(n, ctx->num_sms), 256, 0, st>>>(qq, n, out, rtne);
+  auto sg = [&](const void* k) { return stream_grid(k, 256, 0, ctx->num_sms, (n + 255) / 256); };
+  const bool v = aligned16(q);
+#define MB_Q2B(NB, R)                                                                          \
+  (v ? quire_to_bp_kernel<NB, R, true><<<sg((const void*)quire_to_bp_kernel<NB, R, true>), 256, 0, \
+                                          st>>>(qq, n, out)                                    \
+     : quire_to_bp_kernel<NB, R, false><<<sg((const void*)quire_to_bp_kernel<NB, R, false>), 256, \
+                                           0, st>>>(qq, n, out))
+  if (nbits == 16) {
+    if (rtne) MB_Q2B(16, true); else MB_Q2B(16, false);
+  } else {
+    if (rtne) MB_Q2B(32, true); else MB_Q2B(32, false);
+  }
+#undef MB_Q2B
   return launch_rc();
 }
 
 int bp16_to_quire_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* out,
                       cudaStream_t st) {
   if (n == 0) return RC_OK;
-  bp16_to_quire_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(
-      x, n, reinterpret_cast<quire256*>(out));
+  auto* o = reinterpret_cast<quire256*>(out);
+  const size_t work = (2 * n + 255) / 256;                 // two lanes per code
+  if (aligned16(out))
+    bp16_to_quire_kernel<true><<<stream_grid((const void*)bp16_to_quire_kernel<true>, 256, 0,
+                                             ctx->num_sms, work), 256, 0, st>>>(x, n, o);
+  else
+    bp16_to_quire_kernel<false><<<stream_grid((const void*)bp16_to_quire_kernel<false>, 256, 0,
+                                              ctx->num_sms, work), 256, 0, st>>>(x, n, o);
   return launch_rc();
 }
 
 int int32_to_bp32_run(DeviceContext* ctx, const int32_t* in, size_t n, int shift, uint32_t* out,
                       int rtne, cudaStream_t st) {
   if (n == 0) return RC_OK;
-  int32_to_bp32_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(in, n, shift, out, rtne);
+  if (shift < 0 || shift > 31) {
+    int32_to_bp32_kernel<<<grid_for(n, ctx->num_sms), 256, 0, st>>>(in, n, shift, out, rtne);
+    return launch_rc();
+  }
+  const size_t nv = (aligned16(in) && aligned16(out)) ? n / 4 : 0;
+  const size_t work = ((nv ? nv : n) + 255) / 256;
+  if (rtne)
+    int32_to_bp32_tab_kernel<true><<<stream_grid((const void*)int32_to_bp32_tab_kernel<true>, 256, 0,
+                                                 ctx->num_sms, work), 256, 0, st>>>(in, n, nv, shift, out);
+  else
+    int32_to_bp32_tab_kernel<false><<<stream_grid((const void*)int32_to_bp32_tab_kernel<false>, 256,
+                                                  0, ctx->num_sms, work), 256, 0, st>>>(in, n, nv, shift, out);
   return launch_rc();
 }
 
 int float_to_bposit_run(DeviceContext* ctx, const void* x, int dtype, size_t n, void* out,
                         int nbits, int rtne, cudaStream_t st) {
   if (n == 0) return RC_OK;
-  const unsigned g = grid_for(n, ctx->num_sms);
   if (dtype == MOSYNE_DT_F32) {
-    if (nbits == 16)
-      float_to_bp_kernel<float, 16><<<g, 256, 0, st>>>(static_cast<const float*>(x), n, out, rtne);
-    else
-      float_to_bp_kernel<float, 32><<<g, 256, 0, st>>>(static_cast<const float*>(x), n, out, rtne);
+    const float* xf = static_cast<const float*>(x);
+    // 16-byte input vectors; the output vector is 8 (bposit16) or 16 bytes
+    const bool v = aligned16(x) && (reinterpret_cast<uintptr_t>(out) & (nbits == 16 ? 7u : 15u)) == 0;
+    const size_t nv = v ? n / 4 : 0;
+    const size_t work = ((nv ? nv : n) + 255) / 256;
+#define MB_F2B(NB, R)                                                                          \
+  float_to_bp_f32_kernel<NB, R><<<stream_grid((const void*)float_to_bp_f32_kernel<NB, R>, 256, 0, \
+                                              ctx->num_sms, work), 256, 0, st>>>(xf, n, nv, out)
+    if (nbits == 16) {
+      if (rtne) MB_F2B(16, true); else MB_F2B(16, false);
+    } else {
+      if (rtne) MB_F2B(32, true); else MB_F2B(32, false);
+    }
+#undef MB_F2B
   } else if (dtype == MOSYNE_DT_F64) {
+    const unsigned g = grid_for(n, ctx->num_sms);
     if (nbits == 16)
       float_to_bp_kernel<double, 16><<<g, 256, 0, st>>>(static_cast<const double*>(x), n, out, rtne);
     else

@@ -55,6 +55,46 @@ void h_from_double(const double* x, size_t n, int nbits, int rtne, uint32_t* out
     out[i] = nbits == 16 ? bp::from_double<16>(x[i], rtne) : bp::from_double<32>(x[i], rtne);
 }
 
+void h_from_float(const float* x, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = nbits == 16 ? bp::from_float<16>(x[i], rtne) : bp::from_float<32>(x[i], rtne);
+}
+
+// Mismatches of the int64 sum (bp::sum16_trunc) against the quire path over
+// every code a paired with each b in bs, and with the codes next to -a and a
+// (cancellation and doubling).
+size_t h_sum16_check(const uint16_t* bs, size_t nb) {
+  auto ref = [](uint32_t a, uint32_t b) {
+    return bp::from_quire<16>(bp::q_add(bp::quire_from_bp16(a), bp::quire_from_bp16(b)), false);
+  };
+  size_t bad = 0;
+  for (uint32_t a = 0; a < 65536; ++a) {
+    for (size_t j = 0; j < nb; ++j)
+      if (bp::sum16_trunc(a, bs[j]) != ref(a, bs[j])) ++bad;
+    const uint32_t na = (0u - a) & 0xFFFFu;
+    for (int d = -3; d <= 3; ++d) {
+      const uint32_t b1 = (na + (uint32_t)d) & 0xFFFFu, b2 = (a + (uint32_t)d) & 0xFFFFu;
+      if (bp::sum16_trunc(a, b1) != ref(a, b1)) ++bad;
+      if (bp::sum16_trunc(a, b2) != ref(a, b2)) ++bad;
+    }
+  }
+  return bad;
+}
+
+void h_from_float_tab(const float* x, size_t n, int nbits, int rtne, uint32_t* out) {
+  bp::F32Entry t16[256], t32[256];
+  for (int i = 0; i < 256; ++i) {
+    t16[i] = bp::f32_table_entry<16>(i);
+    t32[i] = bp::f32_table_entry<32>(i);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    if (nbits == 16)
+      out[i] = rtne ? bp::from_float_tab<16, true>(x[i], t16) : bp::from_float_tab<16, false>(x[i], t16);
+    else
+      out[i] = rtne ? bp::from_float_tab<32, true>(x[i], t32) : bp::from_float_tab<32, false>(x[i], t32);
+  }
+}
+
 void h_quire_sum(const uint16_t* p, size_t n, uint64_t* w) {
   bp::quire256 acc = bp::q_zero();
   for (size_t i = 0; i < n; ++i) acc = bp::q_add(acc, bp::quire_from_bp16(p[i]));

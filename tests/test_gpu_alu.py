@@ -66,6 +66,9 @@ def test_binary_ops_random(cuda_lib):
     b = rng.integers(0, 65536, 30000).astype(np.uint16)
     a[:8] = [0, 0x8000, 0x4000, 0, 0x7FFF, 0x0001, 0xFFFF, 0x8001]
     b[:8] = [0x8000, 0, 0x1234, 0, 0x7FFF, 0x0001, 0x8001, 0xFFFF]
+    # cancellation: b next to -a (every third pair is checked below)
+    d = rng.integers(-2, 3, 9000)
+    b[8:9008] = ((65536 - a[8:9008].astype(np.int64) + d) & 0xFFFF).astype(np.uint16)
     add = _u(ops.bposit16_op("add", _t(a), _t(b)))
     mex = _u(ops.bposit16_op("mul_exact", _t(a), _t(b)))
     mul = _u(ops.bposit16_op("mul", _t(a), _t(b)))

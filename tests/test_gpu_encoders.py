@@ -93,6 +93,32 @@ def test_float_to_bposit(cuda_lib, golden):
                 assert np.array_equal(got, exp), (dt, nb, mode)
 
 
+@pytest.mark.parametrize("M,N", [(256, 48), (130, 7)])
+def test_epilogue_i32(cuda_lib, M, N):
+    """The standalone epilogue over a column-major INT32 accumulator (the
+    K-split's exact sum): M % 4 == 0 takes the 16-byte vector kernel, other
+    M the per-element one; bposit32/16 in both roundings, fp32 and bf16
+    dequant, per-row and scalar scales."""
+    from mosyne_bposit import ops
+    rng = np.random.default_rng(24)
+    acc = rng.integers(-(2 ** 31), 2 ** 31, (M, N)).astype(np.int32)
+    acc[0, :4] = [0, 1, -1, -(2 ** 31)]
+    acc[1, :3] = [2 ** 31 - 1, 1 << 24, -(1 << 24) - 1]
+    xs = (rng.random(M) + 0.5).astype(np.float32)
+    ws = (rng.random(N) + 0.5).astype(np.float32)
+    a_t, xs_t, ws_t = torch.from_numpy(acc).cuda(), torch.from_numpy(xs).cuda(), torch.from_numpy(ws).cuda()
+    y_ref = O.dequant(acc.astype(np.int64), xs, ws)
+    for mode in O.MODES:
+        r = ops.epilogue_i32(a_t, bp32=True, bp16=True, y_dtype=torch.float32, x_scale=xs_t,
+                             w_scale=ws_t, rtne32=(mode == "rtne"), rtne16=(mode == "rtne"))
+        assert np.array_equal(_u(r["bp32"], 32), O.encode_int_array(acc.astype(np.int64), 0, 32, mode))
+        assert np.array_equal(_u(r["bp16"], 16), O.encode_int_array(acc.astype(np.int64), 0, 16, mode))
+        assert np.array_equal(r["y"].cpu().numpy().view(np.uint32), y_ref.view(np.uint32))
+    rb = ops.epilogue_i32(a_t, bp32=False, y_dtype=torch.bfloat16, x_scale=xs_t[:1], w_scale=ws_t)
+    y1 = O.dequant(acc.astype(np.int64), np.full(M, xs[0], np.float32), ws)
+    assert torch.equal(rb["y"].cpu(), torch.from_numpy(y1).to(torch.bfloat16))
+
+
 def test_empty_inputs(cuda_lib):
     from mosyne_bposit import ops
     z = torch.empty((0,), dtype=torch.int32, device="cuda")

@@ -103,6 +103,14 @@ def test_per_tensor_quantisation(cuda_lib):
     assert np.array_equal(q_c.cpu().numpy(), xq)
     wqd, wsd = ops.quantize_per_tensor(w.t().contiguous().cuda())     # [N,K] rows
     assert np.array_equal(wqd.cpu().numpy(), wq.T)
+    # more than 2048 rows (warp-per-row kernel, rows walked last to first,
+    # a partial last block of rows)
+    t = torch.randn(4100, 68, generator=torch.Generator().manual_seed(3))
+    tq, ts = O.quant_per_tensor(t.numpy())
+    q_t, s_t = ops.quantize_per_tensor(t.cuda())
+    assert np.array_equal(q_t.cpu().numpy(), tq)
+    q_tc, _ = ops.quantize_per_tensor(t.t().contiguous().cuda(), col_major=True)
+    assert np.array_equal(q_tc.cpu().numpy(), tq)
     r = ops.linear_w8a8(x.cuda(), wqd, wsd, per_tensor=True, bp32=True)
     acc = O.gemm_exact(xq, wq)
     y_ref = O.dequant(acc, np.full(M, xs, np.float32), np.full(N, ws, np.float32))
@@ -112,7 +120,11 @@ def test_per_tensor_quantisation(cuda_lib):
 
 def test_per_token_quantiser_layouts(cuda_lib):
     from mosyne_bposit import ops
-    for (M, K) in [(1, 16), (3, 5), (130, 1000), (2048, 4096)]:
+    # row lengths for every register-resident variant (1, 2, 4, 8, 16 vectors
+    # per thread), the two-pass fallback beyond them, odd K, and M % 4 != 0
+    # (the column-major scalar kernels) next to M % 4 == 0 (vector kernels)
+    for (M, K) in [(1, 16), (3, 5), (130, 1000), (2048, 4096), (132, 2052), (5, 9000),
+                   (12, 20000), (64, 1028)]:
         x, _ = _inputs(M, K, 1, seed=M, outliers=True)
         xq, xs = O.quant_per_token(x.numpy())
         for tdt in (torch.float32, torch.bfloat16, torch.float16):

@@ -59,7 +59,7 @@ def test_int32_fast_path(hlib):
             assert np.array_equal(out, exp.astype(np.uint32)), (nb, rtne)
 
 
-@pytest.mark.parametrize("shift", [0, 6, 12, 24, 31])
+@pytest.mark.parametrize("shift", list(range(32)))
 def test_int32_table_path(hlib, shift):
     """The epilogue's table-driven encoder equals the oracle on every scale
     (each power of two and its neighbours) and on random values, for the
@@ -71,7 +71,7 @@ def test_int32_table_path(hlib, shift):
             v = (1 << b) + d
             if 0 < v < 2 ** 31:
                 edges += [v, -v]
-    I = np.concatenate([rng.integers(-(2 ** 31), 2 ** 31, 200000), np.array(edges),
+    I = np.concatenate([rng.integers(-(2 ** 31), 2 ** 31, 40000), np.array(edges),
                         np.array([0, -(2 ** 31), 2 ** 31 - 1])]).astype(np.int32)
     for nb in (16, 32):
         for rtne in (0, 1):
@@ -117,6 +117,48 @@ def test_double_encoder(hlib):
             hlib.h_from_double(_p(x), ctypes.c_size_t(x.size), nb, rtne, _p(out))
             exp = O.float_to_bposit_array(x, nb, "rtne" if rtne else "truncate").astype(np.uint32)
             assert np.array_equal(out, exp), (nb, rtne)
+
+
+def test_float_encoder(hlib):
+    """The single-precision encoder (32-bit arithmetic) equals the oracle's
+    exact encoding of the same values: normals over the whole exponent range
+    (saturating beyond +-2^48), subnormals, zeros, inf/nan, and the
+    neighbours of every power of two in range."""
+    rng = np.random.default_rng(16)
+    bits = rng.integers(0, 2 ** 32, 60000, dtype=np.uint64).astype(np.uint32)
+    edges = []
+    for e in range(-60, 61):
+        f = np.float32(2.0 ** e)
+        edges += [f, np.nextafter(f, np.float32(0)), np.nextafter(f, np.float32(np.inf))]
+    x = np.concatenate([bits.view(np.float32), np.array(edges, dtype=np.float32),
+                        -np.array(edges, dtype=np.float32),
+                        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 3.4e38],
+                                 dtype=np.float32)])
+    finite = np.isfinite(x)
+    for nb in (16, 32):
+        for rtne in (0, 1):
+            out = np.empty(x.size, dtype=np.uint32)
+            hlib.h_from_float(_p(x), ctypes.c_size_t(x.size), nb, rtne, _p(out))
+            exp = O.float_to_bposit_array(x[finite].astype(np.float64), nb,
+                                          "rtne" if rtne else "truncate").astype(np.uint32)
+            assert np.array_equal(out[finite], exp), (nb, rtne)
+            assert np.all(out[~finite] == (1 << (nb - 1))), (nb, rtne)   # NaR
+            tab = np.empty(x.size, dtype=np.uint32)
+            hlib.h_from_float_tab(_p(x), ctypes.c_size_t(x.size), nb, rtne, _p(tab))
+            assert np.array_equal(tab, out), (nb, rtne)   # table form == direct form
+
+
+def test_sum16_int64_path(hlib):
+    """The ALU's int64 bposit16 sum equals the quire path (itself pinned to
+    the oracle) for every code against 300 partners -- special codes, the
+    extremes of the regime range, random codes -- and against the codes next
+    to -a and a."""
+    rng = np.random.default_rng(17)
+    special = [0, 0x8000, 0x0001, 0xFFFF, 0x7FFF, 0x8001, 0x4000, 0xC000, 0x0002, 0x7FFE,
+               0x0100, 0xFF00, 0x3FFF, 0x4001]
+    bs = np.array(special + list(rng.integers(0, 65536, 300 - len(special))), dtype=np.uint16)
+    hlib.h_sum16_check.restype = ctypes.c_size_t
+    assert hlib.h_sum16_check(_p(bs), ctypes.c_size_t(bs.size)) == 0
 
 
 def test_headline_sum(hlib, golden):
