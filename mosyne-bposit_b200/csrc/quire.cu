@@ -61,41 +61,6 @@ __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * 256, code_sext < 0 ? -V : V);
 }
 
-// The same accumulation with the regime read from a table: the top 8 bits
-// of the 15-bit magnitude fix the regime whenever they are not all equal
-// (run length 1..7, k = -7 .. 6), so a 256-entry table gives the shift that
-// brings the exponent to the top (18 + run length, low byte) and the
-// regime's column offset (k - kGroupLow) * 256 (upper bits).  Entries 0x00
-// and 0xFF (zero, NaR and regimes of 8 or more bits) hold 0 and take the
-// general decode.  The table sits in shared memory as 16 copies per entry,
-// copy = lane & 15, so a warp's lookups conflict at most two ways.
-constexpr int kRegimeLutCopies = 16;
-constexpr int kRegimeLutBytes = 256 * kRegimeLutCopies * 4;     // 16 KiB
-
-__device__ __forceinline__ uint32_t regime_lut_entry(uint32_t hi8) {
-  if (hi8 == 0u || hi8 == 0xFFu) return 0u;
-  const uint32_t lead = hi8 >> 7;
-  const uint32_t y = hi8 << 24;
-  const int rs = __clz(y ^ (y << 1)) + 1;                 // 1..7: the run ends inside
-  const int k = lead ? rs - 1 : -rs;
-  return (uint32_t)(18 + rs) | ((uint32_t)((k - kGroupLow) * 256) << 8);
-}
-
-__device__ __forceinline__ void group_accumulate_lut(int* g, const uint32_t* lut, uint32_t copy,
-                                                     int code_sext) {
-  const uint32_t a = (uint32_t)abs(code_sext) & 0x7FFFu;
-  const uint32_t ent = lut[((a >> 7) * kRegimeLutCopies) | copy];
-  const uint32_t sa = ent & 0xFFu;
-  if (sa == 0u) {
-    group_accumulate_bp16(g, code_sext);
-    return;
-  }
-  const uint32_t z = a << sa;
-  const uint32_t e = z >> 29;
-  const int V = (int)((((z >> 18) & 0x7FFu) | 0x800u) << e);
-  atomicAdd(g + (ent >> 8), code_sext < 0 ? -V : V);
-}
-
 __device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
 #pragma unroll 1
   for (int i = 0; i < kGroups; ++i) {
@@ -143,15 +108,10 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
   __shared__ bool is_last;
-  extern __shared__ int groups[];                         // [kGroups][256], then the table
+  extern __shared__ int groups[];                         // [kGroups][256]
   int* g = groups + threadIdx.x;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(groups + kGroups * 256);
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) g[i * 256] = 0;
-  for (int i = threadIdx.x; i < 256 * kRegimeLutCopies; i += blockDim.x)
-    lut[i] = regime_lut_entry((uint32_t)i / kRegimeLutCopies);
-  __syncthreads();
-  const uint32_t copy = threadIdx.x & (kRegimeLutCopies - 1);
   quire256 acc = bp::q_zero();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -166,8 +126,8 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        group_accumulate_lut(g, lut, copy, (int)(w[j] << 16) >> 16);
-        group_accumulate_lut(g, lut, copy, (int)w[j] >> 16);
+        group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
+        group_accumulate_bp16(g, (int)w[j] >> 16);
       }
       if (++iters == kFoldIters) {
         acc = fold_groups(g, acc);
@@ -399,7 +359,7 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
                        uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
                        int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
-  constexpr int kSumSmem = kGroups * 256 * sizeof(int) + kRegimeLutBytes;   // 43 KiB
+  constexpr int kSumSmem = kGroups * 256 * sizeof(int);         // 27 KiB
   static bool attr_done[kMaxDevices] = {};
   if (!attr_done[ctx->device]) {
     if (cudaFuncSetAttribute(quire_sum_bp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -78,6 +78,31 @@ def test_exact_sum_every_code(cuda_lib):
     assert b16 == 0x7FFF
 
 
+def test_exact_sum_large_inputs(cuda_lib):
+    """Millions of codes: every code (zero, NaR, both extremes of the regime
+    range) many times over, a sign-cancelling mix, an unaligned start with an
+    odd length, and the whole input in a single block."""
+    rng = np.random.default_rng(41)
+    allc = np.tile(np.arange(65536, dtype=np.uint16), 33)
+    rng.shuffle(allc)
+    q, b16, b32 = _sum(allc)
+    ref = O.quire_sum_bposit16(allc)
+    assert q == ref and b16 == O.quire_to_bposit(ref, 16) and b32 == O.quire_to_bposit(ref, 32)
+    pos = rng.integers(1, 0x8000, 1 << 20).astype(np.uint16)
+    mixed = np.concatenate([pos, ((65536 - pos.astype(np.int64)) & 0xFFFF).astype(np.uint16),
+                            np.array([0x4000, 0x0001, 0x7FFF], dtype=np.uint16)])
+    rng.shuffle(mixed)
+    q, _, _ = _sum(mixed)
+    assert q == O.quire_sum_bposit16(mixed)
+    from mosyne_bposit import ops
+    _, codes = O.exact_sum_inputs((1 << 21) + 13, seed=9)
+    x = torch.from_numpy(codes.view(np.int16).copy()).cuda()
+    qd, _, _ = ops.quire_sum_bp16(x[3:])                # 6-byte offset: no 16-byte vectors
+    assert O.words_to_quire(qd.cpu().numpy().view(np.uint64)) == O.quire_sum_bposit16(codes[3:])
+    q1, _, _ = _sum(codes, max_blocks=1)
+    assert q1 == O.quire_sum_bposit16(codes)
+
+
 def test_unaligned_and_empty(cuda_lib):
     from mosyne_bposit import ops
     _, codes = O.exact_sum_inputs(5001, seed=5)
