@@ -216,6 +216,8 @@ def extra_workloads(steps, warmup, peaks, select=None):
     * ffn: the W8A8 SwiGLU FFN of a 3B model at M=2048 (2048 -> 11008 -> 2048):
       quantise, fused gate/up GEMM with the activation in its epilogue,
       re-quantise, down GEMM (tensor-bound; torch bf16 FFN timed beside it);
+    * dec: decode-like GEMMs (M = 32 / 128 rows, K up to 11008) -> bposit32,
+      cuBLASLt INT8 beside (HBM-bound: the weights dominate);
     * bp8: the bposit8 path at 4096^3 -- decode both operands (bposit8 ->
       int8 fixed point) and one fused GEMM whose epilogue encodes acc / 2^12.
     ``select`` (a set of those names) limits the run to some of them."""
@@ -312,6 +314,21 @@ def extra_workloads(steps, warmup, peaks, select=None):
             "us_per_call": ms * 1e3, "tpops": ffn_ops / ms / 1e9,
             "frac_of_int8_peak": ffn_ops / ms / 1e9 / (2.0 * peaks["bf16"]), "bound": "tensor",
             "torch_bf16_us_per_call": bms * 1e3, "launches_per_call": 4}
+    if want("dec"):
+        # decode-like GEMMs (few rows, long K): the single-CTA kernel slices K
+        # over clusters; cuBLASLt INT8 (INT32 out) on the same shapes beside
+        from mosyne_bposit import _api
+        lib = _api.load_library()
+        for (M, N, K) in ((128, 4096, 11008), (32, 4096, 4096), (128, 2048, 8192)):
+            ms, _, _ = _time_gemm(M, N, K, steps, warmup, None, 500 + M,
+                                  lambda A, B, o, st: _ours(A, B, o, st, lib))
+            lms, _, _ = _time_gemm(M, N, K, steps, warmup, None, 600 + M, _cublas_i8)
+            out[f"decode_gemm_{M}x{N}x{K}"] = {
+                "us_per_launch": ms / steps * 1e3, "tpops": 2.0 * M * N * K / (ms / steps) / 1e9,
+                "cublaslt_int8_int32_out_us": lms / steps * 1e3,
+                "bytes_per_launch": M * K + N * K + M * N * 4,
+                "frac_of_hbm": (M * K + N * K + M * N * 4) / (ms / steps) / 1e6 / hbm,
+                "bound": "hbm", "outputs": "bposit32 column-major"}
     if want("bp8"):
         # bposit8 operands (uniform codes) rotated over > 3x L2
         M = N = K = 4096
@@ -702,7 +719,7 @@ def main():
     ap.add_argument("--gemm-flags", type=lambda v: int(v, 0), default=0,
                     help="flags word passed to mosyne_bposit_gemm_i8 with --only-gemm "
                          "(e.g. 0x100000 * (1 + cut) pins the last-wave cut)")
-    ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,bp8|all",
+    ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,dec,bp8|all",
                     help="run only these secondary workloads and print them (for profilers)")
     ap.add_argument("--kernels", action="store_true",
                     help="run only the element-wise / quantiser kernel table (for profilers)")

@@ -56,8 +56,6 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.ffn_h_i8);
   cudaFree(c.ffn_h_scale);
   cudaFree(c.ffn_amax);
-  cudaFree(c.splitk_ws);
-  cudaFree(c.splitk_cnt);
   c = DeviceContext();
 }
 

@@ -38,11 +38,6 @@ struct DeviceContext {
   size_t ffn_h_scale_bytes = 0;
   uint32_t* ffn_amax = nullptr;
   size_t ffn_amax_bytes = 0;
-  // split-K partial tiles and per-tile arrival counters of the single-CTA GEMM
-  int32_t* splitk_ws = nullptr;
-  size_t splitk_ws_bytes = 0;
-  unsigned* splitk_cnt = nullptr;
-  size_t splitk_cnt_bytes = 0;
   bool scratch_ok = true;          // false: entry points that must not allocate
   // bposit16 ALU tables, 65,536 x u16 each, device resident
   uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]

@@ -258,11 +258,12 @@ def test_gemm_bposit8_in_bposit32_out(cuda_lib):
     assert _api.last_error() == 0
 
 
-@pytest.mark.parametrize("split", [2, 3, 5])
+@pytest.mark.parametrize("split", [2, 3, 5, 7])
 @pytest.mark.parametrize("M,N,K,path", [(128, 1100, 2048, 3), (77, 600, 1040, 2), (300, 520, 1536, 3)])
 def test_gemm_single_cta_split_k(cuda_lib, M, N, K, path, split):
-    """Single-CTA kernel with K cut into slices whose exact INT32 partials the
-    last slice of each tile combines: every output kind, both layouts."""
+    """Single-CTA kernel with K cut into slices run as one cluster per tile,
+    the exact INT32 partials summed through distributed shared memory: every
+    output kind, both layouts, slices of one or two k-blocks."""
     from mosyne_bposit import _api, ops
     A = _rand_i8((M, K), split)
     B = _rand_i8((N, K), split + 10)
@@ -283,10 +284,29 @@ def test_gemm_single_cta_split_k(cuda_lib, M, N, K, path, split):
         r = ops.gemm_i8(Ad, Bd, bp32=True, bp16=True, i32=True, rtne32=True, **kw)
         assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
         assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32, "rtne"))
-    # repeated calls reuse the arrival counters
+    # repeated calls
     for _ in range(3):
         r = ops.gemm_i8(Ad, Bd, bp32=False, i32=True, path=path, split=split)
         assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+    assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 4096, 4096), (128, 4096, 11008), (1, 2048, 8192),
+                                   (128, 11008, 2048)])
+def test_gemm_decode_shapes_auto_split(cuda_lib, M, N, K):
+    """Decode-like shapes (few rows, long K) where the kernel picks K slices
+    itself: bposit32 and fp32 outputs against the oracle."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((M, K), 21)
+    B = _rand_i8((N, K), 22)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) + 0.5
+    ws = torch.rand(N, dtype=torch.float32) + 0.5
+    r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=True, y_dtype=torch.float32, x_scale=xs.cuda(),
+                    w_scale=ws.cuda(), row_major=True)
+    assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+    y = O.dequant(acc, xs.numpy(), ws.numpy())
+    assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32))
     assert _api.last_error() == 0
 
 
