@@ -423,6 +423,12 @@ def kernel_table(steps, warmup, peaks):
     row("quire_to_bp32_2^22", lambda: ops.quire_to_bposit(q, 32), 36 * nq)
     row("quire_to_bp16_rtne_2^22", lambda: ops.quire_to_bposit(q, 16, rtne=True), 34 * nq)
     del q, codes
+    ne = 1 << 24                                         # probabilities in (0, 1): 32 MiB of codes
+    pc = torch.randint(1, 0x4000, (ne,), device="cuda", generator=g,
+                       dtype=torch.int32).to(torch.int16)
+    row("shannon_entropy_bp16_2^24", lambda: ops.shannon_entropy_bp16(pc), 2 * ne,
+        note="term table bposit16(p * log2(p)) gathered per code, exact quire256 sum")
+    del pc
     b8 = torch.randint(0, 256, (1 << 27,), device="cuda", generator=g,
                        dtype=torch.int32).to(torch.uint8)
     row("bposit8_to_int8_2^27", lambda: ops.bposit8_to_int8(b8), 2 << 27)

@@ -204,6 +204,27 @@ int mosyne_bposit_quire_sum_bp16(const uint16_t* x, size_t n, mosyne_quire256* q
                                  uint16_t* bp16_out, uint32_t* bp32_out, int flags,
                                  mosyne_stream_t stream);
 
+/* Shannon entropy H = -sum_i p_i log2(p_i) of n bposit16 probabilities
+ * (kernels/shannon_entropy_bposit16.cu:63-119; bposit16_reference.py:813-824):
+ * every p is mapped through the term table bposit16(p * log2(p))
+ * (build_bposit_luts.py:102-110), the negated terms are summed exactly in
+ * quire256 in one grid-wide launch, and the quire is written with its
+ * bposit32 / bposit16 encodings (any output may be NULL; truncating unless
+ * MOSYNE_RTNE_BP32 / MOSYNE_RTNE_BP16).  Asynchronous on `stream`; n == 0
+ * gives H = 0.  Returns 0 or a negative MOSYNE_RC_* code. */
+int mosyne_bposit_shannon_entropy_bp16(const uint16_t* p, size_t n, mosyne_quire256* q_out,
+                                       uint32_t* bp32_out, uint16_t* bp16_out, int flags,
+                                       mosyne_stream_t stream);
+
+/* The reference's entropy entry point, same name, arguments and return codes
+ * (kernels/shannon_entropy_bposit16.cu:124-146): d_p and d_out are device
+ * pointers, *d_out = bposit32(H) (truncating quire256 -> bposit32).  Returns
+ * -1 for n == 0, -2 when the library cannot set up the device, -3 on a launch
+ * or execution error, 0 on success.  Like the reference (whose cudaFree of its
+ * scratch waits for the device), it returns once the result is written: it
+ * runs on the legacy default stream and synchronises it. */
+int shannon_entropy_bposit16_cuda(const uint16_t* d_p, size_t n, uint32_t* d_out);
+
 /* kernels/test_determinism_headline.cu:56-60: fp32 atomicAdd control sum
  * into *acc (not zeroed by the call). */
 int mosyne_bposit_fp32_atomic_sum(const float* x, size_t n, float* acc, mosyne_stream_t stream);

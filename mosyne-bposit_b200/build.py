@@ -40,7 +40,8 @@ def nvcc() -> str:
 def gen_tables(force: bool = False) -> Path:
     GEN.mkdir(parents=True, exist_ok=True)
     out = GEN / "bposit16_tables.inc"
-    if force or not out.exists():
+    src = PKG / "_tables.py"
+    if force or not out.exists() or out.stat().st_mtime < src.stat().st_mtime:
         sys.path.insert(0, str(HERE))
         from mosyne_bposit import _tables
         tmp = out.with_suffix(".tmp")

@@ -19,7 +19,9 @@
 #include "quant.cuh"
 #include "quire.cuh"
 
-#include "_gen/bposit16_tables.inc"  // kBposit16Tables[4][65536], generated at build time
+#include "_gen/bposit16_tables.inc"  // kBposit16Tables[MB_LUT_COUNT][65536], generated at build time
+static_assert(sizeof(kBposit16Tables) == sizeof(uint16_t) * 65536 * mb::MB_LUT_COUNT,
+              "the generated tables and the device table ids disagree");
 
 #ifndef MOSYNE_BPOSIT_VERSION
 #define MOSYNE_BPOSIT_VERSION "0.1.0-b200"
@@ -575,6 +577,25 @@ int mosyne_bposit_quire_sum_bp16(const uint16_t* x, size_t n, mosyne_quire256* q
   if (!ctx) return RC_NOT_INIT;
   return quire_sum_bp16_run(ctx, x, n, q_out, bp16_out, bp32_out, flags, as_stream(stream),
                             (flags >> 16) & 0xFFFF);
+}
+
+int mosyne_bposit_shannon_entropy_bp16(const uint16_t* p, size_t n, mosyne_quire256* q_out,
+                                       uint32_t* bp32_out, uint16_t* bp16_out, int flags,
+                                       mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  return shannon_entropy_bp16_run(ctx, p, n, q_out, bp16_out, bp32_out, flags, as_stream(stream),
+                                  (flags >> 16) & 0xFFFF);
+}
+
+int shannon_entropy_bposit16_cuda(const uint16_t* d_p, size_t n, uint32_t* d_out) {
+  if (n == 0) return -1;
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return -2;
+  if (!d_p || !d_out) return -3;
+  if (shannon_entropy_bp16_run(ctx, d_p, n, nullptr, nullptr, d_out, 0, nullptr) != RC_OK)
+    return -3;
+  return cudaStreamSynchronize(nullptr) == cudaSuccess ? 0 : -3;
 }
 
 int mosyne_bposit_fp32_atomic_sum(const float* x, size_t n, float* acc, mosyne_stream_t stream) {

@@ -43,7 +43,7 @@ struct DeviceContext {
   uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]
 };
 
-enum LutId { LUT_LOG2 = 0, LUT_EXP2 = 1, LUT_SQRT = 2, LUT_RECIP = 3, MB_LUT_COUNT = 4 };
+enum LutId { LUT_LOG2 = 0, LUT_EXP2 = 1, LUT_SQRT = 2, LUT_RECIP = 3, LUT_TERM = 4, MB_LUT_COUNT = 5 };
 
 constexpr int kMaxDevices = 64;
 

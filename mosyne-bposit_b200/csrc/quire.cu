@@ -102,8 +102,19 @@ __device__ __forceinline__ quire256 block_reduce_q(quire256 q, quire256* sh /*[3
   return q;  // valid in thread 0
 }
 
+// TERM: each code p is replaced by -term[p] before it is summed, so the
+// quire holds H = -sum p log2(p) (kernels/shannon_entropy_bposit16.cu:63-119,
+// bposit16_reference.py:813-824: the term table lookup, its quire value,
+// negation, accumulation).  NaR terms add nothing, as bposit16 -> quire maps
+// NaR to zero (bposit16_reference.py:602-605).
+__device__ __forceinline__ int term_summand(uint32_t code, const uint16_t* __restrict__ term) {
+  return -(int)(int16_t)__ldg(term + code);
+}
+
+template <bool TERM>
 __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
-    const uint16_t* __restrict__ x, size_t n, quire256* __restrict__ partials,
+    const uint16_t* __restrict__ x, size_t n, const uint16_t* __restrict__ term,
+    quire256* __restrict__ partials,
     unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
@@ -126,8 +137,13 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
-        group_accumulate_bp16(g, (int)w[j] >> 16);
+        if (TERM) {
+          group_accumulate_bp16(g, term_summand(w[j] & 0xFFFFu, term));
+          group_accumulate_bp16(g, term_summand(w[j] >> 16, term));
+        } else {
+          group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
+          group_accumulate_bp16(g, (int)w[j] >> 16);
+        }
       }
       if (++iters == kFoldIters) {
         acc = fold_groups(g, acc);
@@ -136,7 +152,8 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
     }
     done = nv * 8;
   }
-  for (size_t i = done + tid; i < n; i += stride) group_accumulate_bp16(g, (int)(int16_t)x[i]);
+  for (size_t i = done + tid; i < n; i += stride)
+    group_accumulate_bp16(g, TERM ? term_summand(x[i], term) : (int)(int16_t)x[i]);
   acc = fold_groups(g, acc);
 
   acc = block_reduce_q(acc, sh);
@@ -355,32 +372,51 @@ unsigned grid_for(size_t n, int num_sms, int per_sm = 8) {
 
 }  // namespace
 
-int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
-                       uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
-                       int max_blocks) {
+namespace {
+
+template <bool TERM>
+int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint16_t* term,
+                     mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out, int flags,
+                     cudaStream_t st, int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
   constexpr int kSumSmem = kGroups * 256 * sizeof(int);         // 27 KiB
   static bool attr_done[kMaxDevices] = {};
   if (!attr_done[ctx->device]) {
-    if (cudaFuncSetAttribute(quire_sum_bp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSumSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(quire_sum_bp16_kernel<TERM>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSumSmem) != cudaSuccess)
       return RC_LAUNCH;
     attr_done[ctx->device] = true;
   }
   size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
   // every block resident at once (shared memory bounds the blocks per SM)
-  size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel, 256, kSumSmem,
+  size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel<TERM>, 256, kSumSmem,
                                        ctx->num_sms);
   if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
     return RC_ALLOC;
-  quire_sum_bp16_kernel<<<(unsigned)blocks, 256, kSumSmem, st>>>(
-      x, n, static_cast<quire256*>(ctx->partials), ctx->ticket,
+  quire_sum_bp16_kernel<TERM><<<(unsigned)blocks, 256, kSumSmem, st>>>(
+      x, n, term, static_cast<quire256*>(ctx->partials), ctx->ticket,
       reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
       (flags & MOSYNE_RTNE_BP32) != 0);
   return launch_rc();
+}
+
+}  // namespace
+
+int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
+                       uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
+                       int max_blocks) {
+  return quire_sum_launch<false>(ctx, x, n, nullptr, q_out, bp16_out, bp32_out, flags, st,
+                                 max_blocks);
+}
+
+int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
+                             mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out,
+                             int flags, cudaStream_t st, int max_blocks) {
+  return quire_sum_launch<true>(ctx, p, n, ctx->lut + (size_t)LUT_TERM * 65536, q_out, bp16_out,
+                                bp32_out, flags, st, max_blocks);
 }
 
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,

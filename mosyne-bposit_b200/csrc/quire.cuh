@@ -7,6 +7,11 @@ namespace mb {
 int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
                        uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
                        int max_blocks = 0);
+// H = -sum over p of quire(term[p]) (the Shannon entropy of bposit16
+// probabilities, exact up to the final encode), in one exact-sum launch.
+int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
+                             mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out,
+                             int flags, cudaStream_t st, int max_blocks = 0);
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
                         cudaStream_t st);
 int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void* out, int nbits,

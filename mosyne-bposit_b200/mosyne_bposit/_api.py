@@ -76,6 +76,9 @@ _SIGS = {
     "mosyne_bposit_quantize_with_max": (_I, [_P, _I, _I, _I, _P, _P, _P, _I, _P]),
     "mosyne_bposit_quire_sum_bp16": (_I, [_P, _SZ, _P, _P, _P, _I, _P]),
     "mosyne_bposit_fp32_atomic_sum": (_I, [_P, _SZ, _P, _P]),
+    "mosyne_bposit_shannon_entropy_bp16": (_I, [_P, _SZ, _P, _P, _P, _I, _P]),
+    # kernels/shannon_entropy_bposit16.cu:124: the reference's entropy symbol
+    "shannon_entropy_bposit16_cuda": (_I, [_P, _SZ, _P]),
     "mosyne_bposit_quire_to_bp16": (_I, [_P, _SZ, _P, _I, _P]),
     "mosyne_bposit_quire_to_bp32": (_I, [_P, _SZ, _P, _I, _P]),
     "mosyne_bposit_bp16_to_quire": (_I, [_P, _SZ, _P, _P]),
@@ -324,6 +327,15 @@ def quire_sum_bp16_dev(x: int, n: int, *, q_out: int = 0, bp16_out: int = 0, bp3
     lib = _ensure_library()
     _check(lib.mosyne_bposit_quire_sum_bp16(x, n, q_out, bp16_out, bp32_out, flags, stream),
            "mosyne_bposit_quire_sum_bp16")
+
+
+def shannon_entropy_bp16_dev(p: int, n: int, *, q_out: int = 0, bp32_out: int = 0,
+                             bp16_out: int = 0, flags: int = 0, stream: int = 0) -> None:
+    """H = -sum p log2(p) of n bposit16 codes at device address ``p``
+    (kernels/shannon_entropy_bposit16.cu:63-119), asynchronous on ``stream``."""
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_shannon_entropy_bp16(p, n, q_out, bp32_out, bp16_out, flags, stream),
+           "mosyne_bposit_shannon_entropy_bp16")
 
 
 def fp32_atomic_sum_dev(x: int, n: int, acc: int, *, stream: int = 0) -> None:

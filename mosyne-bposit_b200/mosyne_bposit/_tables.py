@@ -1,4 +1,5 @@
-"""Build-time generator of the bposit16 ALU tables (log2, exp2, sqrt, recip).
+"""Build-time generator of the bposit16 ALU tables (log2, exp2, sqrt, recip,
+term).
 
 The tables follow the reference's definitions exactly
 (kernels/build_bposit_luts.py:34-259 over kernels/bposit16_reference.py):
@@ -11,6 +12,9 @@ The tables follow the reference's definitions exactly
   (bposit16_reference.py:562-584)
 * ``recip[p]`` = bposit16(1 / value(p)) computed exactly; 0/NaR -> NaR
   (bposit16_reference.py:587-599)
+* ``term[p]``  = bposit16(p * log2(p)): NaR where ``log2[p]`` is NaR, else the
+  truncated exact product of ``p`` and ``log2[p]`` (kernels/build_bposit_luts.py:
+  102-110 with bposit16_reference.py:507-516) -- the Shannon-entropy term
 
 Float results enter the encoder the way the reference's boundary conversion
 does: ``Fraction(x).limit_denominator(10**12)`` and then the truncating
@@ -27,7 +31,7 @@ from fractions import Fraction
 
 NAR = 0x8000
 ONE = 0x4000
-TABLE_ORDER = ("log2", "exp2", "sqrt", "recip")   # device table index order
+TABLE_ORDER = ("log2", "exp2", "sqrt", "recip", "term")   # device table index order
 
 
 def value16(p: int):
@@ -128,23 +132,42 @@ def _recip(p):
     return encode16(1 / v)
 
 
+def _mul_exact(a: int, b: int) -> int:
+    """Truncated exact product; zero is checked before NaR
+    (bposit16_reference.py:507-516)."""
+    va, vb = value16(a), value16(b)
+    if va == 0 or vb == 0:
+        return 0
+    if va is None or vb is None:
+        return NAR
+    return encode16(va * vb)
+
+
+def _term_table(log2: list) -> list:
+    return [NAR if lg == NAR else _mul_exact(p, lg) for p, lg in enumerate(log2)]
+
+
 _FUNCS = {"log2": _log2, "exp2": _exp2, "sqrt": _sqrt, "recip": _recip}
 
 
 def build_table(name: str) -> list:
+    if name == "term":
+        return _term_table(build_table("log2"))
     f = _FUNCS[name]
     return [f(p) for p in range(65536)]
 
 
 def build_all() -> dict:
-    return {name: build_table(name) for name in TABLE_ORDER}
+    out = {name: build_table(name) for name in TABLE_ORDER if name != "term"}
+    out["term"] = _term_table(out["log2"])
+    return {name: out[name] for name in TABLE_ORDER}
 
 
 def write_c_include(path, tables: dict | None = None) -> None:
-    """Write ``kBposit16Tables[4][65536]`` as a C include file."""
+    """Write ``kBposit16Tables[len(TABLE_ORDER)][65536]`` as a C include file."""
     tables = tables or build_all()
     lines = ["// generated by mosyne_bposit._tables -- do not edit",
-             "static const uint16_t kBposit16Tables[4][65536] = {"]
+             f"static const uint16_t kBposit16Tables[{len(TABLE_ORDER)}][65536] = {{"]
     for name in TABLE_ORDER:
         t = tables[name]
         lines.append("  { // " + name)

@@ -269,6 +269,26 @@ def quire_sum_bp16(x: torch.Tensor, *, rtne16: bool = False, rtne32: bool = Fals
     return q, b16, b32
 
 
+def shannon_entropy_bp16(p: torch.Tensor, *, rtne32: bool = False, rtne16: bool = False,
+                         max_blocks: int = 0):
+    """Shannon entropy H = -sum p log2(p) of bposit16 probabilities (int16 or
+    uint16 codes), every term p * log2(p) taken from the bposit16 term table
+    and summed exactly -> (quire words int64 [4], bposit32 code, bposit16 code)
+    as device tensors (kernels/shannon_entropy_bposit16.cu:63-119; the
+    reference returns the bposit32 code)."""
+    _need_cuda(p)
+    p = p.contiguous()
+    q = torch.empty((4,), dtype=torch.int64, device=p.device)
+    b32 = torch.empty((1,), dtype=torch.int32, device=p.device)
+    b16 = torch.empty((1,), dtype=torch.int16, device=p.device)
+    flags = (_api.RTNE_BP16 if rtne16 else 0) | (_api.RTNE_BP32 if rtne32 else 0) | \
+        ((max_blocks & 0xFFFF) << 16)
+    _api.shannon_entropy_bp16_dev(p.data_ptr(), p.numel(), q_out=q.data_ptr(),
+                                  bp32_out=b32.data_ptr(), bp16_out=b16.data_ptr(), flags=flags,
+                                  stream=_stream(p))
+    return q, b32, b16
+
+
 def fp32_atomic_sum(x: torch.Tensor) -> torch.Tensor:
     """The non-deterministic IEEE control: fp32 atomicAdd of every element."""
     _need_cuda(x)

@@ -587,6 +587,33 @@ def quire_sum_bposit16(p: np.ndarray) -> int:
     return total
 
 
+_TERM_TABLE = None
+
+
+def term_table() -> np.ndarray:
+    """bposit16(p * log2(p)) for every code p (kernels/build_bposit_luts.py:
+    102-110): NaR where log2 is NaR, else the truncated exact product."""
+    global _TERM_TABLE
+    if _TERM_TABLE is None:
+        t = [NAR16 if (lg := log2_16(i)) == NAR16 else mul16_exact(i, lg) for i in range(65536)]
+        _TERM_TABLE = np.asarray(t, dtype=np.uint16)
+    return _TERM_TABLE
+
+
+def shannon_entropy_quire(p: np.ndarray) -> int:
+    """H = -sum quire(term(p_i)) as a quire integer (pyref:813-824; the kernel
+    kernels/shannon_entropy_bposit16.cu:63-119 negates the sum once, which is
+    the same two's-complement value)."""
+    codes = term_table()[np.asarray(p, dtype=np.uint16)]
+    return -quire_sum_bposit16(codes)
+
+
+def shannon_entropy_bposit(p: np.ndarray, nbits: int = 32, mode: str = "truncate") -> int:
+    """bposit encoding of :func:`shannon_entropy_quire` (the reference returns
+    ``quire256_to_bposit32``, truncating: pyref:824, shannon:112-118)."""
+    return quire_to_bposit(shannon_entropy_quire(p), nbits, mode)
+
+
 # ----- determinism headline inputs (det:110-189) ----------------------------
 
 

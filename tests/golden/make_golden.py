@@ -3,7 +3,7 @@
 Run from the repository root, with the reference checked out at
 ``/root/reference`` (or pass its path as the first argument)::
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference [fixture.json ...]]
 
 It reads the reference's known-answer tables as text, calls the
 reference's own Python arithmetic (kernels/bposit16_reference.py) on seeded
@@ -182,18 +182,56 @@ def probe():
             "hashes": hashes[0], "sources": sorted(refs)}
 
 
+def entropy():
+    """Shannon entropy of bposit16 probabilities through the reference's own
+    integer pipeline (kernels/bposit16_reference.py:813-824; the test case of
+    pyref:850-853 first): bposit32 result and the quire it encodes, for
+    uniform and seeded random distributions, mixed codes (zero, NaR,
+    negatives, saturating values) and every bposit16 code."""
+    def case(name, codes):
+        codes = [int(c) & 0xFFFF for c in codes]
+        q = sum(-R.bposit16_to_quire(R.bposit16_mul(p, R.bposit16_log2(p))) for p in codes)
+        bp32 = R.shannon_entropy_bposit16(codes)
+        assert bp32 == R.quire256_to_bposit32(q)
+        return {"name": name, "codes": codes, "bp32": bp32,
+                "quire_words": [f"{x:016x}" for x in O.quire_to_words(q)]}
+    rng = random.Random(20261202)
+    out = [case("uniform4 (pyref:850-853)", [R.encode_bposit16(Fraction(1, 4))] * 4)]
+    for n in (2, 3, 5, 10, 64, 1000):
+        out.append(case(f"uniform{n}", [R.encode_bposit16(Fraction(1, n))] * n))
+    for n in (16, 256, 1024):
+        w = [rng.random() for _ in range(n)]
+        t = sum(w)
+        out.append(case(f"random{n}", [R.encode_bposit16(Fraction(x / t)) for x in w]))
+    out.append(case("mixed512", [rng.randrange(65536) for _ in range(508)] + [0, 0x8000, 0x7FFF, 0x8001]))
+    allc = case("all_codes", range(65536))
+    allc["codes"] = "range(65536)"
+    out.append(allc)
+    return out
+
+
+FIXTURES = {
+    "kat_quire_to_bp16.json": kat_quire_to_bp16,
+    "kat_quire_to_bp32.json": kat_quire_to_bp32,
+    "kat_int32_to_bp32.json": kat_int32_to_bp32,
+    "kat_add.json": lambda: kat_binary("kernels/test_cases_add_inline.h", 21),
+    "kat_mul.json": lambda: kat_binary("kernels/test_cases_mul_inline.h", 24),
+    "kat_unary.json": lambda: {op: kat_unary(f"kernels/test_{op}.cu") for op in ("sqrt", "recip", "exp2")},
+    "probe_hashes.json": probe,
+    "headline.json": headline,
+    "pyref_samples.json": pyref_samples,
+    "lut_sha256.json": lut_hashes,
+    "bposit8.json": bposit8,
+    "kat_entropy.json": entropy,
+}
+
+
 def main():
-    _write("kat_quire_to_bp16.json", kat_quire_to_bp16())
-    _write("kat_quire_to_bp32.json", kat_quire_to_bp32())
-    _write("kat_int32_to_bp32.json", kat_int32_to_bp32())
-    _write("kat_add.json", kat_binary("kernels/test_cases_add_inline.h", 21))
-    _write("kat_mul.json", kat_binary("kernels/test_cases_mul_inline.h", 24))
-    _write("kat_unary.json", {op: kat_unary(f"kernels/test_{op}.cu") for op in ("sqrt", "recip", "exp2")})
-    _write("probe_hashes.json", probe())
-    _write("headline.json", headline())
-    _write("pyref_samples.json", pyref_samples())
-    _write("lut_sha256.json", lut_hashes())
-    _write("bposit8.json", bposit8())
+    """All fixtures, or only those named after the reference path."""
+    only = sys.argv[2:]
+    for name, make in FIXTURES.items():
+        if not only or name in only:
+            _write(name, make())
 
 
 if __name__ == "__main__":

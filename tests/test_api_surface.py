@@ -65,7 +65,7 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 def _header_symbols():
     txt = (ROOT / "include" / "mosyne_bposit.h").read_text()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(mosyne_bposit\w*)\s*\(", txt)))
+    return sorted(set(re.findall(r"\b((?:mosyne_bposit|shannon_entropy_bposit16)\w*)\s*\(", txt)))
 
 
 @pytest.fixture(scope="module")
@@ -85,7 +85,7 @@ def test_library_exports_every_declared_symbol(built_lib):
     missing = [s for s in syms if not hasattr(lib, s)]
     assert not missing, missing
     nm = subprocess.run(["nm", "-D", "--defined-only", str(built_lib)], capture_output=True, text=True)
-    exported = set(re.findall(r"\b(mosyne_bposit\w*)\b", nm.stdout))
+    exported = set(re.findall(r"\b((?:mosyne_bposit|shannon_entropy_bposit16)\w*)\b", nm.stdout))
     assert set(syms) <= exported
 
 
@@ -102,7 +102,9 @@ def test_reference_abi_symbols_present(built_lib):
             "mosyne_bposit_quantize_weight_per_channel", "mosyne_bposit_linear_w8a8",
             "mosyne_bposit_linear_w8a8_bf16", "mosyne_bposit_linear_w8a8_bf16_io",
             "mosyne_bposit_linear_w8a8_fp16", "mosyne_bposit_linear_w8a8_fp16_io",
-            "mosyne_bposit_linear_w8a8_host"]
+            "mosyne_bposit_linear_w8a8_host",
+            # kernels/shannon_entropy_bposit16.cu:124 (the entropy library's export)
+            "shannon_entropy_bposit16_cuda"]
     lib = ctypes.CDLL(str(built_lib))
     for s in ref9:
         assert hasattr(lib, s), s

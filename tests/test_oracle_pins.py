@@ -115,6 +115,28 @@ def test_lut_hashes_oracle(golden):
     assert hashlib.sha256(struct.pack("<262144Q", *words)).hexdigest() == g["to_quire"]
 
 
+def test_shannon_entropy_goldens(golden):
+    """The oracle's entropy (term table + exact sum + truncating bposit32)
+    equals the reference's integer pipeline on every golden case."""
+    for case in golden("kat_entropy.json"):
+        codes = (np.arange(65536, dtype=np.uint16) if case["codes"] == "range(65536)"
+                 else np.asarray(case["codes"], dtype=np.uint16))
+        q = O.shannon_entropy_quire(codes)
+        assert [f"{x:016x}" for x in O.quire_to_words(q)] == case["quire_words"], case["name"]
+        assert O.shannon_entropy_bposit(codes) == case["bp32"], case["name"]
+
+
+def test_build_time_tables_match_oracle(golden):
+    """The tables the library is built from (mosyne_bposit._tables) are the
+    reference's, term table included."""
+    from mosyne_bposit import _tables
+    g = golden("lut_sha256.json")
+    tabs = _tables.build_all()
+    for name in _tables.TABLE_ORDER:
+        assert hashlib.sha256(struct.pack("<65536H", *tabs[name])).hexdigest() == g[name], name
+    assert np.array_equal(np.asarray(tabs["term"], dtype=np.uint16), O.term_table())
+
+
 def test_determinism_headline(golden):
     h = golden("headline.json")
     _, _, codes = O.det_headline_inputs()
