@@ -50,6 +50,7 @@ constexpr int kGroups = 27;
 constexpr int kGroupLow = -12;
 constexpr int kFoldIters = 256;                          // x 8 codes per iteration
 
+template <int BS>   // the block size: stride between one thread's group sums
 __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   const uint32_t rest = (uint32_t)abs(code_sext) & 0x7FFFu;   // zero and NaR: 0
   const uint32_t y = rest << 17;
@@ -58,15 +59,16 @@ __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   const uint32_t e = z >> 29;
   const int V = (int)(((((z >> 18) & 0x7FFu) | 0x800u)) << e);
   const int k = (int)y < 0 ? rs - 1 : -rs;
-  if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * 256, code_sext < 0 ? -V : V);
+  if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * BS, code_sext < 0 ? -V : V);
 }
 
+template <int BS>
 __device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
 #pragma unroll 1
   for (int i = 0; i < kGroups; ++i) {
-    const int s = g[i * 256];
+    const int s = g[i * BS];
     if (s == 0) continue;
-    g[i * 256] = 0;
+    g[i * BS] = 0;
     const int sh = 8 * (i + kGroupLow) + 85;              // -11 .. 197
     uint64_t mag = s < 0 ? (uint64_t)(-(long long)s) : (uint64_t)s;
     int shp = sh;
@@ -102,27 +104,48 @@ __device__ __forceinline__ quire256 block_reduce_q(quire256 q, quire256* sh /*[3
   return q;  // valid in thread 0
 }
 
-// TERM: each code p is replaced by -term[p] before it is summed, so the
-// quire holds H = -sum p log2(p) (kernels/shannon_entropy_bposit16.cu:63-119,
-// bposit16_reference.py:813-824: the term table lookup, its quire value,
-// negation, accumulation).  NaR terms add nothing, as bposit16 -> quire maps
-// NaR to zero (bposit16_reference.py:602-605).
-__device__ __forceinline__ int term_summand(uint32_t code, const uint16_t* __restrict__ term) {
-  return -(int)(int16_t)__ldg(term + code);
+// Summand modes.  SUM_PLAIN: the codes themselves.  SUM_TERM_L2 /
+// SUM_TERM_SMEM: each code p is replaced by -term[p] before it is summed, so
+// the quire holds H = -sum p log2(p) (kernels/shannon_entropy_bposit16.cu:
+// 63-119, bposit16_reference.py:813-824: the term table lookup, its quire
+// value, negation, accumulation); NaR terms add nothing, as bposit16 ->
+// quire maps NaR to zero (bposit16_reference.py:602-605).  The table is
+// read through L1/L2 (small inputs) or first copied whole into the block's
+// shared memory (one 512-thread block per SM), so every lookup is on chip.
+enum SumMode { SUM_PLAIN = 0, SUM_TERM_L2 = 1, SUM_TERM_SMEM = 2 };
+constexpr int kTermTableBytes = 65536 * 2;
+
+template <int MODE>
+__device__ __forceinline__ int summand(uint32_t code, const uint16_t* __restrict__ tab) {
+  if (MODE == SUM_TERM_L2) return -(int)(int16_t)__ldg(tab + code);
+  return -(int)(int16_t)tab[code];
 }
 
-template <bool TERM>
-__global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
+template <int MODE>
+constexpr size_t sum_smem(int bs) {
+  return (size_t)kGroups * bs * sizeof(int) + (MODE == SUM_TERM_SMEM ? kTermTableBytes : 0);
+}
+
+template <int MODE, int BS>
+__global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
     const uint16_t* __restrict__ x, size_t n, const uint16_t* __restrict__ term,
     quire256* __restrict__ partials,
     unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
     uint32_t* bp32_out, int rtne16, int rtne32) {
   __shared__ quire256 sh[32];
   __shared__ bool is_last;
-  extern __shared__ int groups[];                         // [kGroups][256]
-  int* g = groups + threadIdx.x;
+  extern __shared__ __align__(16) uint8_t sum_smem_raw[];   // [kGroups][BS] int, then the table
+  int* g = reinterpret_cast<int*>(sum_smem_raw) + threadIdx.x;
+  const uint16_t* tab = term;
+  if (MODE == SUM_TERM_SMEM) {
+    uint4* dst = reinterpret_cast<uint4*>(sum_smem_raw + (size_t)kGroups * BS * sizeof(int));
+    const uint4* src = reinterpret_cast<const uint4*>(term);
+    for (int i = threadIdx.x; i < kTermTableBytes / 16; i += BS) dst[i] = __ldg(src + i);
+    tab = reinterpret_cast<const uint16_t*>(dst);
+  }
 #pragma unroll
-  for (int i = 0; i < kGroups; ++i) g[i * 256] = 0;
+  for (int i = 0; i < kGroups; ++i) g[i * BS] = 0;
+  if (MODE == SUM_TERM_SMEM) __syncthreads();
   quire256 acc = bp::q_zero();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -137,24 +160,24 @@ __global__ void __launch_bounds__(256) quire_sum_bp16_kernel(
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (TERM) {
-          group_accumulate_bp16(g, term_summand(w[j] & 0xFFFFu, term));
-          group_accumulate_bp16(g, term_summand(w[j] >> 16, term));
+        if (MODE != SUM_PLAIN) {
+          group_accumulate_bp16<BS>(g, summand<MODE>(w[j] & 0xFFFFu, tab));
+          group_accumulate_bp16<BS>(g, summand<MODE>(w[j] >> 16, tab));
         } else {
-          group_accumulate_bp16(g, (int)(w[j] << 16) >> 16);
-          group_accumulate_bp16(g, (int)w[j] >> 16);
+          group_accumulate_bp16<BS>(g, (int)(w[j] << 16) >> 16);
+          group_accumulate_bp16<BS>(g, (int)w[j] >> 16);
         }
       }
       if (++iters == kFoldIters) {
-        acc = fold_groups(g, acc);
+        acc = fold_groups<BS>(g, acc);
         iters = 0;
       }
     }
     done = nv * 8;
   }
   for (size_t i = done + tid; i < n; i += stride)
-    group_accumulate_bp16(g, TERM ? term_summand(x[i], term) : (int)(int16_t)x[i]);
-  acc = fold_groups(g, acc);
+    group_accumulate_bp16<BS>(g, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab) : (int)(int16_t)x[i]);
+  acc = fold_groups<BS>(g, acc);
 
   acc = block_reduce_q(acc, sh);
   if (threadIdx.x == 0) {
@@ -374,29 +397,31 @@ unsigned grid_for(size_t n, int num_sms, int per_sm = 8) {
 
 namespace {
 
-template <bool TERM>
+template <int MODE, int BS>
 int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint16_t* term,
                      mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out, int flags,
                      cudaStream_t st, int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
-  constexpr int kSumSmem = kGroups * 256 * sizeof(int);         // 27 KiB
+  // group sums 27 KiB per 256 threads (+ the 128 KiB term table when staged)
+  constexpr int kSumSmem = (int)sum_smem<MODE>(BS);
+  static_assert(kSumSmem <= 227 * 1024, "shared memory");
   static bool attr_done[kMaxDevices] = {};
   if (!attr_done[ctx->device]) {
-    if (cudaFuncSetAttribute(quire_sum_bp16_kernel<TERM>,
+    if (cudaFuncSetAttribute(quire_sum_bp16_kernel<MODE, BS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSumSmem) != cudaSuccess)
       return RC_LAUNCH;
     attr_done[ctx->device] = true;
   }
-  size_t blocks = (n + 2047) / 2048;  // >= 8 codes per thread
+  size_t blocks = (n + 8 * BS - 1) / (8 * BS);  // >= 8 codes per thread
   // every block resident at once (shared memory bounds the blocks per SM)
-  size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel<TERM>, 256, kSumSmem,
+  size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel<MODE, BS>, BS, kSumSmem,
                                        ctx->num_sms);
   if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
     return RC_ALLOC;
-  quire_sum_bp16_kernel<TERM><<<(unsigned)blocks, 256, kSumSmem, st>>>(
+  quire_sum_bp16_kernel<MODE, BS><<<(unsigned)blocks, BS, kSumSmem, st>>>(
       x, n, term, static_cast<quire256*>(ctx->partials), ctx->ticket,
       reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
       (flags & MOSYNE_RTNE_BP32) != 0);
@@ -408,15 +433,21 @@ int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint
 int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_quire256* q_out,
                        uint16_t* bp16_out, uint32_t* bp32_out, int flags, cudaStream_t st,
                        int max_blocks) {
-  return quire_sum_launch<false>(ctx, x, n, nullptr, q_out, bp16_out, bp32_out, flags, st,
-                                 max_blocks);
+  return quire_sum_launch<SUM_PLAIN, 256>(ctx, x, n, nullptr, q_out, bp16_out, bp32_out, flags,
+                                          st, max_blocks);
 }
 
 int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
                              mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out,
                              int flags, cudaStream_t st, int max_blocks) {
-  return quire_sum_launch<true>(ctx, p, n, ctx->lut + (size_t)LUT_TERM * 65536, q_out, bp16_out,
-                                bp32_out, flags, st, max_blocks);
+  // the staged table pays once its copy (128 KiB per SM, from L2) is small
+  // beside the gathers it saves
+  const uint16_t* term = ctx->lut + (size_t)LUT_TERM * 65536;
+  if (n >= ((size_t)1 << 20))
+    return quire_sum_launch<SUM_TERM_SMEM, 512>(ctx, p, n, term, q_out, bp16_out, bp32_out, flags,
+                                                st, max_blocks);
+  return quire_sum_launch<SUM_TERM_L2, 256>(ctx, p, n, term, q_out, bp16_out, bp32_out, flags, st,
+                                            max_blocks);
 }
 
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
