@@ -154,21 +154,33 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
   if (vec) {
     const size_t nv = n / 8;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
+    // U independent 16-byte loads in flight per thread: the staged-table
+    // mode runs one 512-thread block per SM and needs them to cover the
+    // load latency; positions past the end read as code 0, which adds
+    // nothing in every mode (zero, or the NaR term of zero)
+    constexpr int U = MODE == SUM_TERM_SMEM ? 4 : 1;
     int iters = 0;
-    for (size_t i = tid; i < nv; i += stride) {
-      const uint4 r = __ldcs(xv + i);
-      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    for (size_t i0 = tid; i0 < nv; i0 += U * stride) {
+      uint4 r[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (MODE != SUM_PLAIN) {
-          group_accumulate_bp16<BS>(g, summand<MODE>(w[j] & 0xFFFFu, tab));
-          group_accumulate_bp16<BS>(g, summand<MODE>(w[j] >> 16, tab));
-        } else {
-          group_accumulate_bp16<BS>(g, (int)(w[j] << 16) >> 16);
-          group_accumulate_bp16<BS>(g, (int)w[j] >> 16);
+      for (int u = 0; u < U; ++u)
+        r[u] = (U == 1 || i0 + u * stride < nv) ? __ldcs(xv + i0 + u * stride)
+                                                : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (MODE != SUM_PLAIN) {
+            group_accumulate_bp16<BS>(g, summand<MODE>(w[j] & 0xFFFFu, tab));
+            group_accumulate_bp16<BS>(g, summand<MODE>(w[j] >> 16, tab));
+          } else {
+            group_accumulate_bp16<BS>(g, (int)(w[j] << 16) >> 16);
+            group_accumulate_bp16<BS>(g, (int)w[j] >> 16);
+          }
         }
       }
-      if (++iters == kFoldIters) {
+      if (++iters == kFoldIters / U) {     // every 2048 codes per thread
         acc = fold_groups<BS>(g, acc);
         iters = 0;
       }
