@@ -123,6 +123,9 @@ def _dist():
     import torch.distributed as dist
     rank = int(os.environ["RANK"])
     local = int(os.environ.get("LOCAL_RANK", rank))
+    # stdout carries exactly one JSON line: NCCL's own log lines (its version
+    # banner included) go to stderr unless the caller chose a log file
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                             device_id=torch.device("cuda", local))
