@@ -315,12 +315,21 @@ int mosyne_bposit16_exp2(const uint16_t* a, size_t n, uint16_t* out, mosyne_stre
  * mosyne_bposit_init.  Its scratch is one fixed static device array (about
  * 8.1 MiB, held by every GPU that loads the library until exit): M <= 16384
  * and M*K <= 8 MiB, else -21.  The first call on each device looks that array
- * up (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls share the array: calls that may overlap on the GPU race, so order
- * them on one stream. */
+ * up (cudaGetSymbolAddress) and should come before any stream capture;
+ * cudaDeviceReset on a device that has used it is not supported (the looked-up
+ * address is kept for the life of the process).  All calls share the array:
+ * calls that may overlap on the GPU race, so order them on one stream.  The
+ * return code covers arguments and launches; a device-side wait that gave up
+ * (a wrong y) is reported afterwards by mosyne_bposit_last_error() as -30. */
 int mosyne_bposit_linear_w8a8_noalloc(const float* d_x_fp32, int M, int K, const int8_t* d_w_i8,
                                       const float* d_w_scale, int N, float* d_y_fp32,
                                       mosyne_stream_t stream);
+
+/* Test hook, no counterpart in the reference: the bounded wait that nothing
+ * satisfies (as mosyne_bposit_debug_wait_timeout), recording into the error
+ * word of mosyne_bposit_linear_w8a8_noalloc, so a test can see a give-up on
+ * that path reported by mosyne_bposit_last_error().  Allocates nothing. */
+int mosyne_bposit_debug_noalloc_wait_timeout(unsigned long long limit_ns, mosyne_stream_t stream);
 
 /* Copies one of the device-resident ALU tables (0 log2, 1 exp2, 2 sqrt,
  * 3 recip; 65,536 u16) to host memory, for verification. */

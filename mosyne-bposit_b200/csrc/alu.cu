@@ -151,13 +151,7 @@ int launch_ew(DeviceContext* ctx, const uint16_t* a, const uint16_t* b, size_t n
   const bool stage = table_op && n >= (size_t)ctx->num_sms * 16384;
   if (stage) {
     // one CTA of 1024 threads per SM holding the 128 KiB table
-    static bool attr[kMaxDevices] = {};
-    if (!attr[ctx->device]) {
-      if (cudaFuncSetAttribute(ew_kernel<OP, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               TAB_BYTES) != cudaSuccess)
-        return RC_LAUNCH;
-      attr[ctx->device] = true;
-    }
+    if (ensure_smem_attr((const void*)ew_kernel<OP, true>, TAB_BYTES) != RC_OK) return RC_LAUNCH;
     ew_kernel<OP, true><<<ctx->num_sms, 1024, TAB_BYTES, st>>>(a, b, n, out, t0, t1);
   } else {
     const unsigned blocks = stream_grid((const void*)ew_kernel<OP, false>, 256, 0, ctx->num_sms,

@@ -94,15 +94,7 @@ int bp8_to_i8_run(const uint8_t* in, size_t n, int8_t* out, int num_sms, cudaStr
     if (head > n) head = n;
     nvec = (n - head) / 16;
   }
-  static bool attr_done[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(bp8_to_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kBp8SmemBytes) != cudaSuccess)
-      return RC_LAUNCH;
-    attr_done[dev] = true;
-  }
+  if (ensure_smem_attr((const void*)bp8_to_i8_kernel, kBp8SmemBytes) != RC_OK) return RC_LAUNCH;
   const size_t work = nvec ? nvec : n;
   const unsigned blocks = stream_grid((const void*)bp8_to_i8_kernel, kBp8Threads, kBp8SmemBytes,
                                       num_sms, (work + kBp8Threads - 1) / kBp8Threads);

@@ -141,6 +141,27 @@ int resident_blocks(const void* kernel, int threads, size_t smem, int num_sms) {
   return v;
 }
 
+int ensure_smem_attr(const void* kernel, int bytes) {
+  struct Key {
+    const void* k;
+    int dev;
+    int bytes;
+  };
+  static std::mutex mu;
+  static Key keys[256];
+  static int used = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RC_LAUNCH;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i].k == kernel && keys[i].dev == dev && keys[i].bytes >= bytes) return RC_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return RC_LAUNCH;
+  if (used < 256) keys[used++] = Key{kernel, dev, bytes};
+  return RC_OK;
+}
+
 namespace {
 
 // Streams and events of the pipelined host-buffer GEMM, per device, made on
@@ -318,14 +339,17 @@ const char* mosyne_bposit_version(void) { return MOSYNE_BPOSIT_VERSION " sm_100a
 int mosyne_bposit_last_error(void) {
   DeviceContext* ctx = ctx_current();
   if (cudaDeviceSynchronize() != cudaSuccess) return RC_LAUNCH;
-  if (!ctx) return RC_OK;
+  // the allocation-free path keeps its own error word (no library state)
+  const int rc_noalloc = noalloc_take_error();
+  if (rc_noalloc == RC_LAUNCH) return RC_LAUNCH;
+  if (!ctx) return rc_noalloc;
   int h = 0;
   if (cudaMemcpy(&h, ctx->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return RC_LAUNCH;
   if (h != 0) {
     cudaMemset(ctx->err, 0, sizeof(int));
     return RC_DEVICE_TIMEOUT;
   }
-  return RC_OK;
+  return rc_noalloc;
 }
 
 int mosyne_bposit_debug_wait_timeout(unsigned long long limit_ns, mosyne_stream_t stream) {

@@ -51,6 +51,10 @@ DeviceContext* ctx_current();       // context of the current device, or nullptr
 DeviceContext* ctx_get_or_init();   // initialise lazily (for the new entry points)
 int ensure_scratch(void** ptr, size_t* cur, size_t need);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device),
+// under a lock, so concurrent first calls from several host threads are safe.
+int ensure_smem_attr(const void* kernel, int bytes);
+
 // Blocks of `kernel` (with `threads` threads and `smem` dynamic shared bytes)
 // that are resident at once on the current device: num_sms times the
 // occupancy limit, cached per kernel.  Grid-stride kernels launch at most

@@ -62,4 +62,8 @@ int gemm_i8_batched_fused(const int8_t* A, const int8_t* B, int K, const EpiPara
 
 int debug_wait_run(unsigned long long limit_ns, DeviceContext* ctx, cudaStream_t st);
 
+// Error word of the allocation-free entry point on the current device: read
+// and cleared; RC_DEVICE_TIMEOUT when a bounded wait there gave up.
+int noalloc_take_error();
+
 }  // namespace mb

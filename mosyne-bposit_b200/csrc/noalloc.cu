@@ -15,9 +15,18 @@
 //
 // Set-up: the first call on each device (with that device current) looks the
 // array's device address up with cudaGetSymbolAddress; make that first call
-// before any stream capture.  All calls share the array and each call
-// overwrites it, so calls that overlap on the GPU (concurrent streams, or
-// launches that may run at the same time) race; order them on one stream.
+// before any stream capture.  The address is cached for the life of the
+// process: cudaDeviceReset on a device that has used this entry point is not
+// supported (the cached address would belong to the destroyed context).  All
+// calls share the array and each call overwrites it, so calls that overlap on
+// the GPU (concurrent streams, or launches that may run at the same time)
+// race; order them on one stream.
+//
+// Errors: every device-side wait of the GEMM is bounded; a wait that gives up
+// records its code in an error word that lives in the same static array, and
+// mosyne_bposit_last_error() reports it (-30) and clears it.  The entry point
+// itself returns before its kernels run, so its return code covers argument
+// and launch errors only.
 #include <cstdio>
 #include <mutex>
 
@@ -35,6 +44,7 @@ struct NoAllocScratch {
   int8_t x_i8[kNoAllocMaxQuantBytes];
   float x_scale[kNoAllocMaxRows];
   uint32_t amax[kNoAllocMaxRows];
+  int err;                 // device error word of this path (0: no wait gave up)
 };
 
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
@@ -66,9 +76,49 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
 }
 
 }  // namespace
+
+// Reads and clears the error word of the allocation-free path on the current
+// device (0 when that path has not run there).  No allocation: a copy from the
+// static array to a host int and a kernel-free memset of one word.
+int noalloc_take_error() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return RC_OK;
+  NoAllocScratch* s = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    s = g_noalloc_dev[dev].scratch;
+  }
+  if (!s) return RC_OK;
+  int h = 0;
+  if (cudaMemcpy(&h, &s->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return RC_LAUNCH;
+  if (h == 0) return RC_OK;
+  if (cudaMemset(&s->err, 0, sizeof(int)) != cudaSuccess) return RC_LAUNCH;
+  return RC_DEVICE_TIMEOUT;
+}
+
+// The bounded wait that nothing satisfies, recording into this path's error
+// word: lets a test see a give-up reported without hanging or faulting a GPU.
+int noalloc_debug_wait(unsigned long long limit_ns, cudaStream_t st) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return RC_LAUNCH;
+  NoAllocDevice* d = nullptr;
+  if (noalloc_setup(dev, &d) != RC_OK) return RC_LAUNCH;
+  DeviceContext ctx;
+  ctx.ready = true;
+  ctx.device = dev;
+  ctx.num_sms = d->num_sms;
+  ctx.err = &d->scratch->err;
+  return debug_wait_run(limit_ns, &ctx, st);
+}
+
 }  // namespace mb
 
 using namespace mb;
+
+extern "C" int mosyne_bposit_debug_noalloc_wait_timeout(unsigned long long limit_ns,
+                                                        mosyne_stream_t stream) {
+  return noalloc_debug_wait(limit_ns, as_stream(stream));
+}
 
 extern "C" int mosyne_bposit_linear_w8a8_noalloc(const float* x, int M, int K, const int8_t* w_i8,
                                                  const float* w_scale, int N, float* y,
@@ -96,7 +146,7 @@ extern "C" int mosyne_bposit_linear_w8a8_noalloc(const float* x, int M, int K, c
   ctx.ready = true;
   ctx.device = dev;
   ctx.num_sms = d->num_sms;
-  ctx.err = nullptr;             // no error word: device waits stay bounded, give-ups are silent
+  ctx.err = &s->err;             // a bounded wait that gives up is reported by last_error
   ctx.scratch_ok = false;        // no split-K workspace: one K slice per tile
   EpiParams p;
   p.M = M;

@@ -417,13 +417,8 @@ int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint
   // group sums 27 KiB per 256 threads (+ the 128 KiB term table when staged)
   constexpr int kSumSmem = (int)sum_smem<MODE>(BS);
   static_assert(kSumSmem <= 227 * 1024, "shared memory");
-  static bool attr_done[kMaxDevices] = {};
-  if (!attr_done[ctx->device]) {
-    if (cudaFuncSetAttribute(quire_sum_bp16_kernel<MODE, BS>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSumSmem) != cudaSuccess)
-      return RC_LAUNCH;
-    attr_done[ctx->device] = true;
-  }
+  if (ensure_smem_attr((const void*)quire_sum_bp16_kernel<MODE, BS>, kSumSmem) != RC_OK)
+    return RC_LAUNCH;
   size_t blocks = (n + 8 * BS - 1) / (8 * BS);  // >= 8 codes per thread
   // every block resident at once (shared memory bounds the blocks per SM)
   size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel<MODE, BS>, BS, kSumSmem,

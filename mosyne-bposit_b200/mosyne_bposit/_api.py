@@ -97,6 +97,7 @@ _SIGS = {
     "mosyne_bposit16_exp2": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit16_table_host": (_I, [_I, _P]),
     "mosyne_bposit_linear_w8a8_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _P, _P]),
+    "mosyne_bposit_debug_noalloc_wait_timeout": (_I, [ctypes.c_ulonglong, _P]),
 }
 
 

@@ -1,7 +1,8 @@
 """Regenerate the golden fixtures in this directory from the reference.
 
-Run from the repository root, with the reference checked out at
-``/root/reference`` (or pass its path as the first argument)::
+Run from the repository root, giving the reference checkout as the first
+argument (else ``$MOSYNE_REFERENCE_ROOT``, else a directory named
+``reference`` beside this repository)::
 
     python tests/golden/make_golden.py [/path/to/reference [fixture.json ...]]
 
@@ -15,6 +16,7 @@ from __future__ import annotations
 import hashlib
 import importlib.util
 import json
+import os
 import random
 import re
 import struct
@@ -24,7 +26,8 @@ from fractions import Fraction
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else
+           os.environ.get("MOSYNE_REFERENCE_ROOT", str(HERE.parents[2] / "reference")))
 KERN = REF / "kernels"
 sys.path.insert(0, str(KERN))
 import bposit16_reference as R  # noqa: E402

@@ -73,3 +73,58 @@ def test_noalloc_rejects_inputs_beyond_its_scratch(cuda_lib):
                                                  s.data_ptr(), 1, y.data_ptr(), None) == -21
     assert lib.mosyne_bposit_linear_w8a8_noalloc(x.data_ptr(), 0, 16, w.data_ptr(),
                                                  s.data_ptr(), 1, y.data_ptr(), None) == -20
+
+
+def _regular_and_noalloc(lib, M, K, N, seed, stream=None):
+    x_cm, w = _case(M, K, N, seed)
+    wq = torch.empty((N, K), dtype=torch.int8, device="cuda")
+    ws = torch.empty((N,), dtype=torch.float32, device="cuda")
+    assert lib.mosyne_bposit_quantize_weight_per_channel(w.data_ptr(), K, N, wq.data_ptr(),
+                                                         ws.data_ptr()) == 0
+    y_ref = torch.empty((N, M), dtype=torch.float32, device="cuda")
+    assert lib.mosyne_bposit_linear_w8a8(x_cm.data_ptr(), M, K, wq.data_ptr(), ws.data_ptr(),
+                                         N, y_ref.data_ptr()) == 0
+    torch.cuda.synchronize()
+    y = torch.full((N, M), float("nan"), dtype=torch.float32, device="cuda")
+    if stream is None:
+        rc = lib.mosyne_bposit_linear_w8a8_noalloc(x_cm.data_ptr(), M, K, wq.data_ptr(),
+                                                   ws.data_ptr(), N, y.data_ptr(), None)
+    else:
+        stream.wait_stream(torch.cuda.current_stream())    # y's fill is done first
+        with torch.cuda.stream(stream):
+            rc = lib.mosyne_bposit_linear_w8a8_noalloc(x_cm.data_ptr(), M, K, wq.data_ptr(),
+                                                       ws.data_ptr(), N, y.data_ptr(),
+                                                       stream.cuda_stream)
+        stream.synchronize()
+    assert rc == 0
+    return y, y_ref
+
+
+def test_noalloc_on_a_caller_stream(cuda_lib):
+    s = torch.cuda.Stream()
+    for seed in (3, 4):                                 # two calls in a row on that stream
+        y, y_ref = _regular_and_noalloc(cuda_lib, 300, 1024, 640, seed, stream=s)
+        assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32))
+
+
+def test_noalloc_at_its_size_limits(cuda_lib):
+    # M = 16384 rows and M*K = 8 MiB exactly: the largest accepted input
+    y, y_ref = _regular_and_noalloc(cuda_lib, 16384, 512, 256, 5)
+    assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32))
+
+
+def test_noalloc_reports_a_wait_that_gave_up(cuda_lib):
+    """A bounded device wait on this path that gives up must not go unseen:
+    the test hook runs the bounded wait that nothing satisfies against this
+    path's error word, and last_error reports -30 once, then clears it."""
+    from mosyne_bposit import _api
+    lib = cuda_lib
+    assert _api.last_error() == 0
+    assert lib.mosyne_bposit_debug_noalloc_wait_timeout(2_000_000, None) == 0
+    assert _api.last_error() == -30
+    assert _api.last_error() == 0
+    # the path still works afterwards
+    y, y_ref = _regular_and_noalloc(lib, 64, 256, 128, 6)
+    assert torch.equal(y.view(torch.int32), y_ref.view(torch.int32))
+    assert _api.last_error() == 0
+
