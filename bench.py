@@ -14,6 +14,12 @@ N > 1 (torchrun, one rank per GPU): column-parallel N-shard -- each rank
 computes its own 4096-column block of an M=4096, K=4096, N=4096*ranks GEMM
 (weak scaling, no collective on the data path); time = max over ranks.
 
+Every N also runs the C5 workload (W8A8 16384 x 8192 x 28672, per-token /
+per-channel scales, fp32 y + bposit32): N-shard as strong scaling and, at
+N > 1, the K-split with an exact INT32 reduce-scatter over NCCL; the
+gathered outputs' SHA-256 are compared with the oracle's committed hashes
+and with the same problem run on one GPU ("c5_16384x8192x28672").
+
 --impl reference: the reference's CPU path for the same workload on the
 host cores (numpy exact integer GEMM + bposit32 encoding of every output,
 the oracle's restatement of kernels/bposit16_reference.py), rank 0 only.
@@ -144,6 +150,17 @@ def _max_over_ranks(dist, v: float) -> float:
     t = torch.tensor([v], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def _all_ranks(dist, v: float) -> list:
+    """v of every rank, in rank order (one all-gather)."""
+    if dist is None:
+        return [v]
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
 
 
 def _time_gemm(M, N, K, steps, warmup, dist, seed, lib_call):
@@ -439,49 +456,152 @@ def kernel_table(steps, warmup, peaks):
     return res
 
 
-def ksplit_workload(dist, ws, steps, warmup):
-    """K-split across the ranks (the exchange the path has): each rank holds a
-    4096-deep K slice of a 4096 x 4096 x (4096 * ranks) GEMM, computes its
-    exact INT32 partial, the partials are summed with an NCCL int32
-    all-reduce (exact: two's-complement addition is associative) and every
-    rank encodes the sum to bposit32.  Times the whole step and the
-    all-reduce alone (CUDA events, slowest rank)."""
+def _sha256_t(t) -> str:
+    """SHA-256 of a device tensor's bytes (copied to the host in 256 MiB pieces)."""
+    import hashlib
+
+    import torch
+    h = hashlib.sha256()
+    flat = t.contiguous().view(torch.uint8).reshape(-1)
+    step = 256 << 20
+    for i in range(0, flat.numel(), step):
+        h.update(flat[i:i + step].cpu().numpy().tobytes())
+    return h.hexdigest()
+
+
+def _c5_golden():
+    p = ROOT / "tests" / "golden" / "c5_hashes.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text())["rows"].get("16384")
+
+
+def c5_workload(dist, ws, rank, steps, warmup, chunks=4):
+    """C5: W8A8 16384 x 8192 x 28672 with per-token activation and
+    per-channel weight scales, fp32 y + bposit32 outputs (column-major), on
+    every rank of the job:
+
+    * N-shard (strong scaling): rank r computes output channels
+      [N r / p, N (r+1) / p) from the whole activation; no collective.
+    * K-split (p > 1): rank r holds K slice r of both operands (global
+      scales by all_reduce(MAX)); exact INT32 partials are reduce-scattered
+      over NCCL in ``chunks`` chunks, each rank encodes the columns it owns.
+
+    Inputs (numpy seed 0, tests/golden/configs.py) are drawn on rank 0 and
+    broadcast.  The timed steps are the GEMM (N-shard) and the whole K-split
+    call (partial GEMMs + reduce-scatter + epilogue); quantisation is done
+    once beforehand, as a weight-stationary layer does.  After timing, the
+    outputs are gathered and their SHA-256 compared with the oracle's
+    (tests/golden/c5_hashes.json) and, at p > 1, with the same problem run
+    on rank 0's GPU alone."""
+    import sys as _sys
+
     import torch
 
     from mosyne_bposit import dist as D
-    M = N = Kr = 4096
-    g = torch.Generator(device="cuda").manual_seed(300 + dist.get_rank())
-    A = torch.randint(-127, 128, (M, Kr), device="cuda", generator=g, dtype=torch.int8)
-    B = torch.randint(-127, 128, (N, Kr), device="cuda", generator=g, dtype=torch.int8)
-    acc = torch.empty((N, M), dtype=torch.int32, device="cuda")
+    from mosyne_bposit import ops
+    _sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import configs
+    M, K, N = configs.C5
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if rank == 0:
+        x, w = configs.c5_inputs()
+        xd, wd = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)
+        del x, w
+    else:
+        xd = torch.empty((M, K), dtype=torch.float32, device=dev)
+        wd = torch.empty((N, K), dtype=torch.float32, device=dev)
+    if dist is not None:
+        dist.broadcast(xd, 0)
+        dist.broadcast(wd, 0)
+    ops_total = 2.0 * M * N * K
+    golden = _c5_golden()
+    out = {"shape": [M, K, N], "inputs": "numpy default_rng(0): x ~ N(0,1), w ~ N(0,0.02)",
+           "outputs": "fp32 y + bposit32, column-major [M,N]", "ranks": ws}
 
-    def step():   # the library's K-split call
-        return D.ksplit_gemm_i8(A, B, bp32=True)
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        _barrier(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        own = e0.elapsed_time(e1) / steps
+        return _max_over_ranks(dist, own), own, r
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
-    dist.barrier()
-    e0.record()
-    for _ in range(steps):
-        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
-    e1.record()
-    torch.cuda.synchronize()
-    ar_ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
-    ops_total = 2.0 * M * N * Kr * ws
-    return {"shape": [M, N, Kr * ws], "ms_per_step": ms, "tpops": ops_total / ms / 1e9,
-            "allreduce_ms": ar_ms, "allreduce_bytes": 4 * M * N,
-            "allreduce_busbw_gbs": 2 * (ws - 1) / ws * 4 * M * N / ar_ms / 1e6,
-            "note": "mosyne_bposit.dist.ksplit_gemm_i8: local GEMM to exact INT32, NCCL int32 "
-                    "all-reduce of the 64 MiB partials, bposit32 epilogue on every rank"}
+    # ---- N-shard
+    n0, n1 = D.shard_range(N, ws, rank)
+    xq, xs = ops.quantize_per_token(xd)
+    wq, wsc = ops.quantize_per_channel(wd[n0:n1])
+    res = {"y": torch.empty((n1 - n0, M), dtype=torch.float32, device=dev).t(),
+           "bp32": torch.empty((n1 - n0, M), dtype=torch.int32, device=dev).t()}
+    ms, own_ms, _ = timed(lambda: ops.gemm_i8(xq, wq, bp32=True, y_dtype=torch.float32,
+                                              x_scale=xs, w_scale=wsc, out=res))
+    out["nshard"] = {"ms_per_step": ms, "tpops": ops_total / ms / 1e9, "rank0_ms": own_ms,
+                     "per_gpu_columns": n1 - n0}
+    hashes = {}
+    for k in ("bp32", "y"):
+        full = D.gather_columns(res[k]) if dist is not None else res[k]
+        if rank == 0:
+            hashes[k] = _sha256_t(full.t())
+        del full
+    if rank == 0:
+        out["nshard"]["sha256"] = hashes
+        if golden:
+            out["nshard"]["bit_identical_to_oracle"] = (hashes["bp32"] == golden["bp32"] and
+                                                        hashes["y"] == golden["y_f32"])
+    del res, wq
+    # ---- K-split
+    if dist is not None:
+        k0, k1 = D.shard_range(K, ws, rank)
+        xq_s, xs_g = D.ksplit_quantize_rows(xd[:, k0:k1].contiguous())
+        wq_s, ws_g = D.ksplit_quantize_rows(wd[:, k0:k1].contiguous())
+
+        def kstep():
+            return D.ksplit_gemm_i8(xq_s, wq_s, bp32=True, y_dtype=torch.float32, x_scale=xs_g,
+                                    w_scale=ws_g, chunks=chunks, gather=False)
+        ms_k, own_k, r = timed(kstep)
+        # the reduce-scatter alone, on buffers of the same size
+        L = D.ksplit_layout(N, ws, chunks)
+        src = torch.zeros((L["padded"], M), dtype=torch.int32, device=dev)
+        dst = torch.empty((L["padded"] // ws, M), dtype=torch.int32, device=dev)
+        ms_rs, _, _ = timed(lambda: dist.reduce_scatter_tensor(dst, src))
+        del src, dst
+        g = D.ksplit_gather(r, N, chunks=chunks, keys=("bp32", "y"))
+        kh = {k: _sha256_t(g[k].t()) for k in ("bp32", "y")} if rank == 0 else {}
+        del g, r
+        out["ksplit"] = {"ms_per_step": ms_k, "tpops": ops_total / ms_k / 1e9, "rank0_ms": own_k,
+                         "chunks": chunks, "reduce_scatter_ms": ms_rs,
+                         "reduce_scatter_bytes_per_rank": 4 * L["padded"] * M,
+                         "reduce_scatter_busbw_gbs": (ws - 1) / ws * 4 * L["padded"] * M / ms_rs / 1e6,
+                         "note": "per step: partial INT32 GEMMs of the K slice, NCCL int32 "
+                                 "reduce-scatter per chunk (overlapping the next chunk's GEMM), "
+                                 "fp32 y + bposit32 epilogue of the owned columns"}
+        if rank == 0:
+            out["ksplit"]["sha256"] = kh
+            if golden:
+                out["ksplit"]["bit_identical_to_oracle"] = (kh["bp32"] == golden["bp32"] and
+                                                            kh["y"] == golden["y_f32"])
+        del xq_s, wq_s
+        # the same problem on rank 0's GPU alone, in this run
+        if rank == 0:
+            wq1, ws1 = ops.quantize_per_channel(wd)
+            r1 = ops.gemm_i8(xq, wq1, bp32=True, y_dtype=torch.float32, x_scale=xs, w_scale=ws1)
+            torch.cuda.synchronize()
+            one = {"bp32": _sha256_t(r1["bp32"].t()), "y": _sha256_t(r1["y"].t())}
+            del r1, wq1
+            out["one_gpu_sha256"] = one
+            out["bit_identical_to_1gpu"] = {"nshard": hashes == one, "ksplit": kh == one}
+        _barrier(dist)
+    if rank == 0 and golden:
+        out["oracle_sha256"] = {"bp32": golden["bp32"], "y": golden["y_f32"]}
+    del xd, wd, xq
+    torch.cuda.empty_cache()
+    return out
 
 
 def _ours(A, B, out, stream, lib, flags=0):
@@ -619,6 +739,7 @@ def run_ours(args):
     ops = 2.0 * M * N * K
     with Clocks(local) as clk:
         ms, nsets, _ = _time_gemm(M, N, K, args.steps, args.warmup, dist, 100 + rank, call)
+    rank_ms = _all_ranks(dist, ms / args.steps)
     ms = _max_over_ranks(dist, ms)
     clocks = clk.summary()
     per_launch_ms = ms / args.steps
@@ -635,7 +756,10 @@ def run_ours(args):
     lib_ms, _, _ = _time_gemm(M, N, K, args.steps, args.warmup, None, 300 + rank, _cublas_i8)
     lib_ms2, _, _ = _time_gemm(M2, N2, K2, args.steps, args.warmup, None, 400 + rank, _cublas_i8)
     e2e = _e2e(M, N, K, max(3, min(args.steps, 10)), lib, dist, ws)
-    ksplit = ksplit_workload(dist, ws, max(3, min(args.steps, 10)), 2) if dist is not None else None
+    c5 = c5_workload(dist, ws, rank, max(3, min(args.steps, 10)), 2)
+    rc = _api.last_error()
+    if rc != 0:
+        raise RuntimeError(f"device error word set during the C5 runs (rc={rc})")
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -643,6 +767,8 @@ def run_ours(args):
     peaks = _peaks()
     peak = 2.0 * peaks["bf16"]
     achieved = ops / (per_launch_ms * 1e-3) / 1e12
+    lib_tpops = ops / (lib_ms / args.steps * 1e-3) / 1e12
+    lib_tpops2 = 2.0 * M2 * N2 * K2 / (lib_ms2 / args.steps * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_launch_ms, "higher_is_better": True,
@@ -669,15 +795,43 @@ def run_ours(args):
                      "kernel": "gemm_i8_tcgen05_pair", "algorithmic": f"2*M*N*K = {ops:.4g} ops per launch"},
         "gpu_launches": args.steps,
         "clocks": clocks,
+        "ms_per_launch_by_rank": rank_ms,
+        # per GPU, this build against cuBLASLt INT8 (INT32 out only) on the same GPU
+        "tpops_per_gpu": {"4096^3": achieved, "2048x14336x4096": v2 / ws},
+        "cublaslt_int8_tpops": {"4096^3": lib_tpops, "2048x14336x4096": lib_tpops2},
+        "vs_cublaslt": {"4096^3": achieved / lib_tpops, "2048x14336x4096": (v2 / ws) / lib_tpops2},
+        "c5_16384x8192x28672": c5,
     }
+    if dist is not None:
+        line["c5_tpops"] = {"nshard": c5["nshard"]["tpops"], "ksplit": c5["ksplit"]["tpops"]}
+        line["bit_identical_to_1gpu"] = c5.get("bit_identical_to_1gpu")
+    else:
+        line["c5_tpops"] = {"one_gpu": c5["nshard"]["tpops"]}
+    line["c5_bit_identical_to_oracle"] = {k: c5[k].get("bit_identical_to_oracle")
+                                          for k in ("nshard", "ksplit") if k in c5}
     line["e2e"] = e2e
-    if ksplit is not None:
-        line["workloads"]["ksplit_4096x4096xK"] = ksplit
     if ws == 1:
         line["workloads"].update(extra_workloads(args.steps, args.warmup, peaks))
         line["kernels"] = kernel_table(args.steps, args.warmup, peaks)
         line["cpu_baseline"] = cpu_baseline(M, N, K)
     print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_only_c5(args):
+    """--only-c5: the C5 workload alone (any N), one JSON line from rank 0."""
+    import torch
+
+    from mosyne_bposit import _api
+    dist, rank, local, ws = _dist()
+    if dist is None:
+        torch.cuda.set_device(0)
+    _api.load_library(init=True)
+    c5 = c5_workload(dist, ws, rank, args.steps, args.warmup, chunks=args.chunks)
+    rc = _api.last_error()
+    if rank == 0:
+        print(json.dumps({"c5_16384x8192x28672": c5, "n_gpus": ws, "device_error": rc}), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
@@ -730,6 +884,9 @@ def main():
                          "(e.g. 0x100000 * (1 + cut) pins the last-wave cut)")
     ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,dec,bp8|all",
                     help="run only these secondary workloads and print them (for profilers)")
+    ap.add_argument("--only-c5", action="store_true",
+                    help="run only the C5 16384x8192x28672 workload (N-shard, K-split, hashes)")
+    ap.add_argument("--chunks", type=int, default=4, help="K-split reduce-scatter chunks (--only-c5)")
     ap.add_argument("--kernels", action="store_true",
                     help="run only the element-wise / quantiser kernel table (for profilers)")
     args = ap.parse_args()
@@ -737,6 +894,8 @@ def main():
         args.warmup = 3
     if args.only_gemm:
         run_only_gemm(args)
+    elif args.only_c5:
+        run_only_c5(args)
     elif args.workloads or args.kernels:
         run_tables(args)
     elif args.impl == "reference":

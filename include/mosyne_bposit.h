@@ -281,6 +281,19 @@ int mosyne_bposit_epilogue_i32(const int32_t* acc, int M, int N, const float* x_
                                const float* w_scale, uint32_t* out_bp32, uint16_t* out_bp16,
                                void* out_y, int y_dtype, int flags, mosyne_stream_t stream);
 
+/* No counterpart in the reference (its quire argument, whitepaper.tex:495-507,
+ * at the width the value needs): exact INT64 accumulators for sums of INT32
+ * partials that may exceed INT32 -- the K-split across GPUs when
+ * 127^2 * K >= 2^31.  widen: dst[i] = (int64) src[i], or dst[i] += src[i]
+ * with accumulate != 0.  epilogue_i64: as mosyne_bposit_epilogue_i32 over an
+ * INT64 accumulator acc [M,N] (column-major); bposit outputs encode
+ * acc / 2^s with flags MOSYNE_BP_SHIFT(s), y = (float)acc / (xs[m] * ws[n]). */
+int mosyne_bposit_widen_i32(const int32_t* src, size_t n, int64_t* dst, int accumulate,
+                            mosyne_stream_t stream);
+int mosyne_bposit_epilogue_i64(const int64_t* acc, int M, int N, const float* x_scale,
+                               const float* w_scale, uint32_t* out_bp32, uint16_t* out_bp16,
+                               void* out_y, int y_dtype, int flags, mosyne_stream_t stream);
+
 /* bposit16 ALU, element-wise over n codes.
  * add: kernels/bposit16_encode.cuh:472-483 (exact via quire256);
  * mul: bposit16_encode.cuh:491-537 (log2 + quire add + exp2 tables);

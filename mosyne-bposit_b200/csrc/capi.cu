@@ -701,6 +701,38 @@ int mosyne_bposit_epilogue_i32(const int32_t* acc, int M, int N, const float* x_
   return epilogue_i32_run(acc, p, ctx, as_stream(stream));
 }
 
+int mosyne_bposit_epilogue_i64(const int64_t* acc, int M, int N, const float* x_scale,
+                               const float* w_scale, uint32_t* out_bp32, uint16_t* out_bp16,
+                               void* out_y, int y_dtype, int flags, mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || N <= 0 || !acc) return RC_BAD_ARG;
+  if (out_y && (!x_scale || !w_scale || !dtype_ok(y_dtype))) return RC_BAD_ARG;
+  EpiParams p;
+  p.M = M;
+  p.N = N;
+  p.xs = x_scale;
+  p.ws = w_scale;
+  p.xs_stride = (flags & MOSYNE_XS_SCALAR) ? 0 : 1;
+  p.ws_stride = (flags & MOSYNE_WS_SCALAR) ? 0 : 1;
+  p.bp32 = out_bp32;
+  p.bp16 = out_bp16;
+  p.y = out_y;
+  p.y_dtype = y_dtype;
+  p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+  p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+  p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  p.bp_shift = (int)(((unsigned)flags >> 24) & 31u);
+  return epilogue_i64_run(acc, p, ctx, as_stream(stream));
+}
+
+int mosyne_bposit_widen_i32(const int32_t* src, size_t n, int64_t* dst, int accumulate,
+                            mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  return widen_i32_run(src, n, dst, accumulate ? 1 : 0, ctx, as_stream(stream));
+}
+
 #define MB_ALU_ENTRY(name, op)                                                           \
   int name(const uint16_t* a, size_t n, uint16_t* out, mosyne_stream_t stream) {         \
     DeviceContext* ctx = ctx_get_or_init();                                              \

@@ -50,6 +50,13 @@ int gemm_i8_run(const int8_t* A, const int8_t* B, int K, const EpiParams& p,
 int epilogue_i32_run(const int32_t* acc, const EpiParams& p, DeviceContext* ctx,
                      cudaStream_t st);
 
+// INT64 accumulators (wide.cu): dst (+)= (int64) src over n elements, and the
+// epilogue over a column-major INT64 accumulator (bposit of acc / 2^bp_shift,
+// (float)acc / (xs * ws) dequant).
+int widen_i32_run(const int32_t* src, size_t n, int64_t* dst, int add, DeviceContext* ctx,
+                  cudaStream_t st);
+int epilogue_i64_run(const int64_t* acc, const EpiParams& p, DeviceContext* ctx, cudaStream_t st);
+
 // Bounded wait that nothing satisfies; sets the device error word.
 // n 32-bit words of device memory set to zero by a kernel (orders correctly
 // before the programmatic-dependent GEMM launches, unlike a memset node).

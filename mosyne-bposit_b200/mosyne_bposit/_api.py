@@ -87,6 +87,8 @@ _SIGS = {
     "mosyne_bposit_ffn_swiglu_w8a8": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I, _P]),
     "mosyne_bposit_float_to_bposit": (_I, [_P, _I, _SZ, _P, _I, _I, _P]),
     "mosyne_bposit_epilogue_i32": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "mosyne_bposit_epilogue_i64": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "mosyne_bposit_widen_i32": (_I, [_P, _SZ, _P, _I, _P]),
     "mosyne_bposit16_add": (_I, [_P, _P, _SZ, _P, _P]),
     "mosyne_bposit16_mul": (_I, [_P, _P, _SZ, _P, _P]),
     "mosyne_bposit16_mul_exact": (_I, [_P, _P, _SZ, _P, _P]),
@@ -390,6 +392,20 @@ def epilogue_i32_dev(acc: int, M: int, N: int, *, x_scale: int = 0, w_scale: int
     lib = _ensure_library()
     _check(lib.mosyne_bposit_epilogue_i32(acc, M, N, x_scale, w_scale, out_bp32, out_bp16, out_y,
                                           y_dtype, flags, stream), "mosyne_bposit_epilogue_i32")
+
+
+def epilogue_i64_dev(acc: int, M: int, N: int, *, x_scale: int = 0, w_scale: int = 0,
+                     out_bp32: int = 0, out_bp16: int = 0, out_y: int = 0, y_dtype: int = DT_F32,
+                     flags: int = 0, stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_epilogue_i64(acc, M, N, x_scale, w_scale, out_bp32, out_bp16, out_y,
+                                          y_dtype, flags, stream), "mosyne_bposit_epilogue_i64")
+
+
+def widen_i32_dev(src: int, n: int, dst: int, *, accumulate: bool = False, stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_widen_i32(src, n, dst, 1 if accumulate else 0, stream),
+           "mosyne_bposit_widen_i32")
 
 
 _ALU1 = {"recip": "mosyne_bposit16_recip", "sqrt": "mosyne_bposit16_sqrt",

@@ -432,6 +432,61 @@ def epilogue_i32(acc: torch.Tensor, *, bp32: bool = True, bp16: bool = False,
     return res
 
 
+def epilogue_i64(acc: torch.Tensor, *, bp32: bool = True, bp16: bool = False,
+                 y_dtype: torch.dtype | None = None, x_scale: torch.Tensor | None = None,
+                 w_scale: torch.Tensor | None = None, rtne32: bool = False,
+                 rtne16: bool = False, scale_shift: int = 0) -> dict:
+    """``epilogue_i32`` over an INT64 accumulator (a logical ``[M,N]`` stored
+    column-major): the exact sum of partials that may not fit INT32."""
+    _need_cuda(acc, x_scale, w_scale)
+    if acc.dtype != torch.int64:
+        raise ValueError("acc must be int64")
+    M, N = acc.shape
+    store = acc.t()
+    if not store.is_contiguous():
+        store = store.contiguous()
+    res = {}
+    if bp32:
+        res["bp32"] = _out((M, N), torch.int32, acc.device, False)
+    if bp16:
+        res["bp16"] = _out((M, N), torch.int16, acc.device, False)
+    if not 0 <= scale_shift <= 31:
+        raise ValueError("scale_shift must be in 0..31")
+    flags = (_api.RTNE_BP32 if rtne32 else 0) | (_api.RTNE_BP16 if rtne16 else 0) | \
+        (scale_shift << 24)
+    if y_dtype is not None:
+        if x_scale is None or w_scale is None:
+            raise ValueError("dequantised output needs x_scale and w_scale")
+        res["y"] = _out((M, N), y_dtype, acc.device, False)
+        if x_scale.numel() == 1:
+            flags |= _api.XS_SCALAR
+        if w_scale.numel() == 1:
+            flags |= _api.WS_SCALAR
+    _api.epilogue_i64_dev(store.data_ptr(), M, N, x_scale=_ptr(x_scale), w_scale=_ptr(w_scale),
+                          out_bp32=_ptr(res.get("bp32")), out_bp16=_ptr(res.get("bp16")),
+                          out_y=_ptr(res.get("y")), y_dtype=_DT[y_dtype] if y_dtype else 0,
+                          flags=flags, stream=_stream(acc))
+    return res
+
+
+def widen_i32(src: torch.Tensor, dst: torch.Tensor | None = None, *,
+              accumulate: bool = False) -> torch.Tensor:
+    """``dst = src`` (or ``dst += src`` with ``accumulate``) as INT64, element
+    by element over same-shaped contiguous tensors; returns ``dst``."""
+    _need_cuda(src, dst)
+    if src.dtype != torch.int32 or not src.is_contiguous():
+        raise ValueError("src must be a contiguous int32 tensor")
+    if dst is None:
+        if accumulate:
+            raise ValueError("accumulate needs dst")
+        dst = torch.empty(src.shape, dtype=torch.int64, device=src.device)
+    if dst.dtype != torch.int64 or not dst.is_contiguous() or dst.numel() != src.numel():
+        raise ValueError("dst must be a contiguous int64 tensor of src's size")
+    _api.widen_i32_dev(src.data_ptr(), src.numel(), dst.data_ptr(), accumulate=accumulate,
+                       stream=_stream(src))
+    return dst
+
+
 def bposit16_op(op: str, a: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
     """Element-wise bposit16 ALU: add, mul, mul_exact (binary); neg,
     neg_ones_complement, recip, sqrt, log2, exp2 (unary)."""

@@ -2,8 +2,9 @@
 
 * ``gpu`` marks tests that need a CUDA device (run on a B200 with
   ``pytest -m gpu``); everything else runs on the CPU.
-* The repository root (for ``oracle``) and ``mosyne-bposit_b200`` (for the
-  ``mosyne_bposit`` package) are put on ``sys.path``.
+* The repository root (for ``oracle``), ``mosyne-bposit_b200`` (for the
+  ``mosyne_bposit`` package) and ``tests/golden`` (for ``configs``, the
+  seeded inputs of the benchmark configurations) are put on ``sys.path``.
 """
 from __future__ import annotations
 
@@ -16,7 +17,7 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 PKG_DIR = ROOT / "mosyne-bposit_b200"
 GOLDEN = Path(__file__).resolve().parent / "golden"
-for p in (str(ROOT), str(PKG_DIR)):
+for p in (str(ROOT), str(PKG_DIR), str(GOLDEN)):
     if p not in sys.path:
         sys.path.insert(0, p)
 

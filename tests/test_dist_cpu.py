@@ -98,6 +98,78 @@ def _worker_ksplit(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
+def _ksplit_case(M, K, N, seed, extreme=False):
+    """Quantised K-split operands (int8 A [M,K], B [N,K]) and scales; with
+    ``extreme`` every code is 127, so INT32 sums overflow beyond K = 133,152."""
+    rng = np.random.default_rng(seed)
+    if extreme:
+        A = np.full((M, K), 127, np.int8)
+        B = np.full((N, K), 127, np.int8)
+        A[::2] = -127
+    else:
+        A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+        B = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    xs = (rng.random(M) + 0.5).astype(np.float32)
+    ws = (rng.random(N) + 0.5).astype(np.float32)
+    return A, B, xs, ws
+
+
+def _worker_ksplit_variants(rank, world, port, q):
+    """reduce-scatter with chunks (gathered and per-rank), all-reduce, and the
+    INT64 partials beyond the INT32 limit; every result equals the exact
+    single-process one."""
+    try:
+        _setup(rank, world, port)
+        from mosyne_bposit import dist as D
+        from oracle import bposit_oracle as O
+        si = _stand_ins()
+        local = {k: si[k] for k in ("local_gemm", "local_epilogue")}
+        report = {}
+        for name, (M, K, N, chunks, reduce, extreme) in {
+                "scatter_c3": (17, 300, 70, 3, "scatter", False),
+                "scatter_c1_uneven": (9, 64, 5, 1, "scatter", False),
+                "all_c2": (12, 96, 33, 2, "all", False),
+                "wide": (6, 140000, 7, 2, "scatter", True)}.items():
+            A, B, xs, ws = _ksplit_case(M, K, N, len(name), extreme)
+            k0, k1 = D.shard_range(K, world, rank)
+            acc = O.gemm_exact(A, B.T)
+            want_bp = O.encode_int_array(acc, 0, 32)
+            want_y = O.dequant(acc, xs, ws)
+            res = D.ksplit_gemm_i8(torch.from_numpy(A[:, k0:k1].copy()),
+                                   torch.from_numpy(B[:, k0:k1].copy()), bp32=True,
+                                   y_dtype=torch.float32, x_scale=torch.from_numpy(xs),
+                                   w_scale=torch.from_numpy(ws), reduce=reduce, chunks=chunks,
+                                   **local)
+            key = "i64" if extreme else "i32"
+            report[name] = (np.array_equal(res[key].numpy().astype(np.int64), acc)
+                            and np.array_equal(res["bp32"].numpy().view(np.uint32), want_bp)
+                            and np.array_equal(res["y"].numpy().view(np.uint32),
+                                               want_y.view(np.uint32)))
+            if reduce == "scatter":
+                own = D.ksplit_gemm_i8(torch.from_numpy(A[:, k0:k1].copy()),
+                                       torch.from_numpy(B[:, k0:k1].copy()), bp32=True,
+                                       reduce=reduce, chunks=chunks, gather=False, **local)
+                bp = own["bp32"].numpy().view(np.uint32)
+                j, ok = 0, True
+                per = D.ksplit_layout(N, world, chunks)["per"]
+                for (a, b) in own["cols"]:
+                    ok &= np.array_equal(bp[:, j:j + b - a], want_bp[:, a:b])
+                    j += per
+                report[name + "_owned"] = bool(ok)
+        if extreme:
+            # the same sums in INT32 would wrap: refused unless wide
+            try:
+                D.ksplit_gemm_i8(torch.from_numpy(A[:, k0:k1].copy()),
+                                 torch.from_numpy(B[:, k0:k1].copy()), wide=False, **local)
+                report["refuses_narrow"] = False
+            except ValueError:
+                report["refuses_narrow"] = True
+        q.put((rank, all(report.values()), report))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e)))
+
+
 def _worker_nshard(rank, world, port, q):
     try:
         _setup(rank, world, port)
@@ -155,6 +227,24 @@ def _run(fn, world=2, timeout=120):
 def test_ksplit_bit_identical_to_single_process():
     out = _run(_worker_ksplit)
     assert all(ok for _, ok, _ in out), out
+
+
+def test_ksplit_reduce_scatter_chunks_and_wide_partials():
+    out = _run(_worker_ksplit_variants, timeout=240)
+    assert all(ok for _, ok, _ in out), out
+
+
+def test_ksplit_layout_partitions_columns():
+    from mosyne_bposit.dist import ksplit_layout, ksplit_owned_columns
+    for N in (1, 7, 70, 1000, 28672):
+        for world in (1, 2, 3, 8):
+            for chunks in (1, 2, 3, 5):
+                L = ksplit_layout(N, world, chunks)
+                assert L["padded"] >= N and L["padded"] % world == 0
+                spans = sorted(r for k in range(world)
+                               for r in ksplit_owned_columns(N, world, k, chunks) if r[1] > r[0])
+                assert spans[0][0] == 0 and spans[-1][1] == N
+                assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
 
 
 def test_nshard_gather_bit_identical():

@@ -2,7 +2,9 @@
 mosyne_bposit.dist on the CUDA library: the K-split linear (global row
 maxima by all_reduce(MAX), exact INT32 partials by all_reduce(SUM)) and the
 column-parallel GEMM with all-gather must equal the one-GPU results bit for
-bit, and the oracle.  Skipped on machines with fewer than two GPUs."""
+bit, and the oracle; the K-split's reduce-scatter (in chunks, gathered or
+kept per rank), its all-reduce form and its INT64 partials (K = 140,000)
+equal the exact single-GPU sums.  Skipped on machines with fewer than two GPUs."""
 from __future__ import annotations
 
 import os
@@ -84,6 +86,41 @@ def _worker(rank, world, port, q):
         acc = O.gemm_exact(A.numpy(), B.numpy().T)
         report["nshard_bp32_vs_oracle"] = np.array_equal(
             full["bp32"].cpu().numpy().view(np.uint32), O.encode_int_array(acc, 0, 32))
+        # K-split variants: reduce-scatter in chunks (gathered and per rank),
+        # all-reduce, and INT64 partials beyond the INT32 range
+        M, K, N = 200, 2048, 1000
+        A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+        B = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+        xs = torch.rand(M, generator=g) + 0.5
+        ws_ = torch.rand(N, generator=g) + 0.5
+        k0, k1 = D.shard_range(K, world, rank)
+        acc = O.gemm_exact(A.numpy(), B.numpy().T)
+        want_bp = O.encode_int_array(acc, 0, 32)
+        want_y = O.dequant(acc, xs.numpy(), ws_.numpy())
+        a_s, b_s = A[:, k0:k1].contiguous().to(dev), B[:, k0:k1].contiguous().to(dev)
+        for reduce, chunks in (("scatter", 1), ("scatter", 3), ("all", 2)):
+            r = D.ksplit_gemm_i8(a_s, b_s, bp32=True, y_dtype=torch.float32, x_scale=xs.to(dev),
+                                 w_scale=ws_.to(dev), reduce=reduce, chunks=chunks)
+            report[f"ksplit_{reduce}_{chunks}"] = (
+                np.array_equal(r["bp32"].cpu().numpy().view(np.uint32), want_bp)
+                and np.array_equal(r["y"].cpu().numpy().view(np.uint32), want_y.view(np.uint32)))
+        own = D.ksplit_gemm_i8(a_s, b_s, bp32=True, chunks=3, gather=False)
+        per = D.ksplit_layout(N, world, 3)["per"]
+        bp = own["bp32"].cpu().numpy().view(np.uint32)
+        report["ksplit_owned_columns"] = all(
+            np.array_equal(bp[:, j * per:j * per + b - a], want_bp[:, a:b])
+            for j, (a, b) in enumerate(own["cols"]))
+        Kw = 140_000
+        Aw = torch.full((64, Kw), 127, dtype=torch.int8)
+        Aw[::2] = -127
+        Bw = torch.full((40, Kw), 127, dtype=torch.int8)
+        k0, k1 = D.shard_range(Kw, world, rank)
+        r = D.ksplit_gemm_i8(Aw[:, k0:k1].contiguous().to(dev), Bw[:, k0:k1].contiguous().to(dev),
+                             bp32=True)
+        accw = O.gemm_exact(Aw.numpy(), Bw.numpy().T)
+        report["ksplit_wide_i64"] = np.array_equal(r["i64"].cpu().numpy(), accw)
+        report["ksplit_wide_bp32"] = np.array_equal(r["bp32"].cpu().numpy().view(np.uint32),
+                                                    O.encode_int_array(accw, 0, 32))
         report["device_error"] = _api.last_error()
         torch.cuda.synchronize()
         dist.barrier()

@@ -223,3 +223,21 @@ def test_bposit8_tables(golden):
         assert [f"{x:016x}" for x in w] == g["to_quire_words"][i], i
         assert O.bposit8_to_int8(i) == g["to_int8"][i], i
     assert O.bposit8_to_int8(0x40) == 64                  # 1.0 -> 2^6
+
+
+def test_c5_golden_hashes_reproduce_on_256_rows(golden):
+    """The committed C5 output hashes come from configs.c5_inputs and the
+    oracle: the first 256 rows (all 28,672 columns, K = 8192) reproduce."""
+    import hashlib
+
+    import configs
+    want = golden("c5_hashes.json")["rows"]["256"]
+    x, w = configs.c5_inputs(256)
+    wq, ws = O.quant_per_channel(w.T)
+    xq, xs = O.quant_per_token(x)
+    acc = O.gemm_exact(xq, wq)                                   # [256, N]
+    at = np.ascontiguousarray(acc.T)
+    bp = np.concatenate([O.encode_int_array(c, 0, 32) for c in np.array_split(at.reshape(-1), 64)])
+    y = np.ascontiguousarray(O.dequant(acc, xs, ws).T)
+    assert hashlib.sha256(bp.tobytes()).hexdigest() == want["bp32"]
+    assert hashlib.sha256(y.tobytes()).hexdigest() == want["y_f32"]
