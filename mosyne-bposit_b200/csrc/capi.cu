@@ -58,6 +58,8 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.ffn_h_i8);
   cudaFree(c.ffn_h_scale);
   cudaFree(c.ffn_amax);
+  cudaFree(c.sk_ws);
+  cudaFree(c.sk_flags);
   c = DeviceContext();
 }
 
@@ -69,12 +71,14 @@ int init_device(int d) {
     return -1;
   if (cudaMalloc(&c.err, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c.ticket, sizeof(unsigned int)) != cudaSuccess ||
-      cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess) {
+      cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess ||
+      cudaMalloc(&c.sk_flags, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess) {
     free_ctx(c);
     return -2;
   }
   if (cudaMemset(c.err, 0, sizeof(int)) != cudaSuccess ||
       cudaMemset(c.ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(c.sk_flags, 0, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
       cudaMemcpy(c.lut, kBposit16Tables, sizeof(kBposit16Tables), cudaMemcpyHostToDevice) !=
           cudaSuccess) {
     free_ctx(c);
@@ -347,6 +351,8 @@ int mosyne_bposit_last_error(void) {
   if (cudaMemcpy(&h, ctx->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return RC_LAUNCH;
   if (h != 0) {
     cudaMemset(ctx->err, 0, sizeof(int));
+    // a wait that gave up may have left stream-K ready flags set
+    cudaMemset(ctx->sk_flags, 0, 2 * kSkMaxPairs * sizeof(unsigned));
     return RC_DEVICE_TIMEOUT;
   }
   return rc_noalloc;
@@ -382,8 +388,9 @@ int mosyne_bposit_gemm_i8(const int8_t* A, const int8_t* B, int M, int N, int K,
   p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
   p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
   p.bp_shift = (flags >> 24) & 31;
-  // test hooks: force a GEMM path / tail cut (bits 16-21) / K slices (bits 29-31)
-  const int path = ((flags >> 16) & 0x3F) | ((int)(((unsigned)flags >> 29) & 0x7u) << 8);
+  // test hooks: force a GEMM path / tail cut (bits 16-21) / stream-K phase off
+  // (bit 22) or on (bit 23) / K slices (bits 29-31)
+  const int path = ((flags >> 16) & 0xFF) | ((int)(((unsigned)flags >> 29) & 0x7u) << 8);
   return gemm_i8_run(A, B, K, p, ctx, as_stream(stream), path);
 }
 

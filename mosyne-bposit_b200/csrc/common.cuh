@@ -39,6 +39,11 @@ struct DeviceContext {
   uint32_t* ffn_amax = nullptr;
   size_t ffn_amax_bytes = 0;
   bool scratch_ok = true;          // false: entry points that must not allocate
+  // stream-K partial tiles of the CTA-pair GEMM ([pair][cta][256 cols][128 rows]
+  // int32) and their per-CTA ready flags (zero between launches)
+  int32_t* sk_ws = nullptr;
+  size_t sk_ws_bytes = 0;
+  unsigned* sk_flags = nullptr;
   // bposit16 ALU tables, 65,536 x u16 each, device resident
   uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]
 };
@@ -85,6 +90,10 @@ constexpr int ERR_MMA_WAIT_TMEM = 3;
 constexpr int ERR_EPI_WAIT = 4;
 constexpr int ERR_DRAIN_WAIT = 5;
 constexpr int ERR_TEST_WAIT = 6;
+constexpr int ERR_SK_WAIT = 7;        // a stream-K partial tile did not arrive
+
+// Upper bound on CTA pairs of the pair GEMM (stream-K flag array size).
+constexpr int kSkMaxPairs = 128;
 
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

@@ -41,7 +41,7 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
             x_scale: torch.Tensor | None = None, w_scale: torch.Tensor | None = None,
             rtne32: bool = False, rtne16: bool = False, row_major: bool = False,
             out: dict | None = None, path: int = 0, tail: int = 0,
-            scale_shift: int = 0, split: int = 0) -> dict:
+            scale_shift: int = 0, split: int = 0, stream_k: bool | None = None) -> dict:
     """Exact ``acc = A @ B^T`` for int8 ``A [M,K]`` and ``B [N,K]`` (both
     K-contiguous) with the requested encodings of every dot product:
     ``bp32``/``bp16`` (bposit of the INT32 value), ``i32``, and ``y`` =
@@ -50,8 +50,10 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
     ``scale_shift`` makes the bposit outputs encode ``acc / 2^scale_shift``.
     ``path`` and ``tail`` pin the kernel choice (tests): path 1 tensor cores,
     2/3 one-CTA tiles 128/256 wide, 4 CUDA cores, 5 CTA pairs; tail 1/2/3 cuts
-    the CTA-pair kernel's last wave into whole/half/quarter tiles; split (1-7)
-    sets the single-CTA kernel's K slices."""
+    the CTA-pair kernel's last wave into whole/half/quarter tiles (and turns
+    its stream-K phase off); ``stream_k`` True/False pins that phase on/off
+    (None: the library's default); split (1-7) sets the single-CTA kernel's K
+    slices."""
     _need_cuda(A, B, x_scale, w_scale)
     if A.dtype != torch.int8 or B.dtype != torch.int8:
         raise ValueError("A and B must be int8")
@@ -84,7 +86,8 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, bp16: bool =
         raise ValueError("scale_shift must be in 0..31")
     if not 0 <= split <= 7:
         raise ValueError("split must be in 0..7")
-    flags |= ((path & 0xF) << 16) | ((tail & 0x3) << 20) | (scale_shift << 24) | (split << 29)
+    flags |= ((path & 0xF) << 16) | ((tail & 0x3) << 20) | (scale_shift << 24) | (split << 29) | \
+        (0 if stream_k is None else (1 << 23 if stream_k else 1 << 22))
     if flags >= 1 << 31:
         flags -= 1 << 32                                   # the C ABI takes a signed int
     _api.gemm_i8_dev(A.data_ptr(), B.data_ptr(), M, N, K,

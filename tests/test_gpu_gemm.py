@@ -383,3 +383,66 @@ def test_gemm_batched_one_launch(cuda_lib, b, M, N, K):
             y3 = O.dequant(acc, np.full(M, 1.5, np.float32), ws[h].numpy())
             assert np.array_equal(_np(r3["y"][h].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y3))
     assert _api.last_error() == 0
+
+
+def _check_stream_k(M, N, K, seed=11):
+    """The CTA-pair kernel's stream-K phase (k-block ranges of the last tiles
+    shared over all pairs, exact INT32 partial tiles combined by the pair
+    that owns each tile) against the oracle and against the same kernel
+    without it, for every single output and fp32 + bposit32 together."""
+    from mosyne_bposit import _api, ops
+    A = _rand_i8((M, K), seed)
+    B = _rand_i8((N, K), seed + 1)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) * 3 + 0.01
+    ws = torch.rand(N, dtype=torch.float32) * 2 + 0.01
+    Ad, Bd, xd, wd = A.cuda(), B.cuda(), xs.cuda(), ws.cuda()
+    y = O.dequant(acc, xs.numpy(), ws.numpy())
+    for rm in (False, True):
+        kw = dict(row_major=rm, path=5, stream_k=True)
+        for rt in (False, True):
+            r = ops.gemm_i8(Ad, Bd, bp32=True, rtne32=rt, **kw)
+            want = O.encode_int_array(acc, 0, 32, "rtne" if rt else "truncate")
+            assert np.array_equal(_np(r["bp32"], np.uint32), want), (M, N, K, rm, rt)
+        r = ops.gemm_i8(Ad, Bd, bp32=True, y_dtype=torch.float32, x_scale=xd, w_scale=wd, **kw)
+        assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), (M, N, K, rm)
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+        r = ops.gemm_i8(Ad, Bd, bp32=False, y_dtype=torch.bfloat16, x_scale=xd, w_scale=wd, **kw)
+        assert np.array_equal(_np(r["y"].view(torch.int16), np.uint16), O.f32_to_bf16_bits(y))
+        r = ops.gemm_i8(Ad, Bd, bp32=False, bp16=True, i32=True, **kw)
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+        assert np.array_equal(_np(r["bp16"], np.uint16), O.encode_int_array(acc, 0, 16))
+        r2 = ops.gemm_i8(Ad, Bd, bp32=False, i32=True, **dict(kw, stream_k=False))
+        assert np.array_equal(_np(r2["i32"]).astype(np.int64), acc)
+    # repeated launches reuse the workspace and its ready flags
+    for _ in range(3):
+        r = ops.gemm_i8(Ad, Bd, bp32=True, path=5, stream_k=True)
+    assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+    assert _api.last_error() == 0
+
+
+# (all tiles stream-K, ~14 k-blocks a pair), (whole waves then a stream-K
+# phase of one wave plus the partial one), (ragged M, N, K), (fewer tiles
+# than pairs, K of 2 k-blocks)
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 2048), (4096, 5120, 1024), (1000, 3000, 4112),
+                                   (700, 900, 256), (512, 4608, 8192)])
+def test_gemm_pair_stream_k(cuda_lib, M, N, K):
+    _check_stream_k(M, N, K)
+
+
+def test_gemm_batched_stream_k(cuda_lib):
+    from mosyne_bposit import ops
+    b, M, N, K = 3, 300, 500, 640
+    A = _rand_i8((b, M, K), 21)
+    B = _rand_i8((b, N, K), 22)
+    xs = torch.rand(b, M) + 0.5
+    ws = torch.rand(b, N) + 0.5
+    r = ops.gemm_i8_batched(A.cuda(), B.cuda(), bp32=True, y_dtype=torch.float32,
+                            x_scale=xs.cuda(), w_scale=ws.cuda())
+    torch.cuda.synchronize()
+    for z in range(b):
+        acc = O.gemm_exact(A[z].numpy(), B[z].numpy().T)
+        assert np.array_equal(_np(r["bp32"][z], np.uint32), O.encode_int_array(acc, 0, 32))
+        y = O.dequant(acc, xs[z].numpy(), ws[z].numpy())
+        assert np.array_equal(_np(r["y"][z]).view(np.uint32), y.view(np.uint32))
+

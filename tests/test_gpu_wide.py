@@ -67,7 +67,7 @@ def test_long_k_partials_in_int64_match_exact_sum(cuda_lib):
     A = torch.full((M, K), 127, dtype=torch.int8)
     A[::3] = -127
     B = torch.full((N, K), 127, dtype=torch.int8)
-    B[:, ::7] = -1
+    B[::5] = -127                                    # |sums| = 127^2 * K > 2^31
     Ad, Bd = A.cuda(), B.cuda()
     acc64 = torch.empty((N, M), dtype=torch.int64, device="cuda")
     tmp = torch.empty((N, M), dtype=torch.int32, device="cuda")
@@ -77,7 +77,7 @@ def test_long_k_partials_in_int64_match_exact_sum(cuda_lib):
                     out={"i32": tmp.t()})
         ops.widen_i32(tmp, acc64, accumulate=j > 0)
     want = O.gemm_exact(A.numpy(), B.numpy().T)
-    assert want.max() > 2 ** 31                      # beyond INT32
+    assert np.abs(want).max() > 2 ** 31              # beyond INT32
     assert np.array_equal(acc64.t().cpu().numpy(), want)
     r = ops.epilogue_i64(acc64.t(), bp32=True)
     assert np.array_equal(r["bp32"].cpu().numpy().view(np.uint32), O.encode_int_array(want, 0, 32))
