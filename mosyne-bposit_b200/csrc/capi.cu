@@ -60,6 +60,7 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.ffn_amax);
   cudaFree(c.sk_ws);
   cudaFree(c.sk_flags);
+  cudaFree(c.pt_bar);
   c = DeviceContext();
 }
 
@@ -72,13 +73,15 @@ int init_device(int d) {
   if (cudaMalloc(&c.err, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c.ticket, sizeof(unsigned int)) != cudaSuccess ||
       cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess ||
-      cudaMalloc(&c.sk_flags, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess) {
+      cudaMalloc(&c.sk_flags, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
+      cudaMalloc(&c.pt_bar, 4 * sizeof(unsigned)) != cudaSuccess) {
     free_ctx(c);
     return -2;
   }
   if (cudaMemset(c.err, 0, sizeof(int)) != cudaSuccess ||
       cudaMemset(c.ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
       cudaMemset(c.sk_flags, 0, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c.pt_bar, 0, 4 * sizeof(unsigned)) != cudaSuccess ||
       cudaMemcpy(c.lut, kBposit16Tables, sizeof(kBposit16Tables), cudaMemcpyHostToDevice) !=
           cudaSuccess) {
     free_ctx(c);
@@ -237,6 +240,10 @@ int linear_impl(const void* x, int x_dtype, int M, int K, const int8_t* w_i8,
   p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
   p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
   p.rtne16 = (flags & MOSYNE_RTNE_BP16) ? 1 : 0;
+  // the quantiser just launched started after every earlier kernel of the
+  // stream finished, and lets the GEMM start early: the weights are final
+  // then, so the GEMM may pull them into L2 while the activation is quantised
+  p.b_prefetch = 1;
   rc = gemm_i8_run(ctx->x_i8, w_i8, K, p, ctx, st);
   return rc == RC_BAD_ARG ? RC_BAD_ARG : (rc ? RC_GEMM : RC_OK);
 }

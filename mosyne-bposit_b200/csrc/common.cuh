@@ -28,6 +28,9 @@ struct DeviceContext {
   void* partials = nullptr;        // exact-sum block partials
   size_t partials_bytes = 0;
   unsigned int* ticket = nullptr;  // last-block ticket for grid reductions
+  // grid barrier of the one-launch per-tensor quantiser: [0] arrivals,
+  // [1] generation, [2 + (generation & 1)] that call's |max| (fp32 bits)
+  unsigned int* pt_bar = nullptr;
   // SwiGLU FFN intermediates: activation [M,F] fp32, its int8 codes, scales
   // and row maxima
   float* ffn_act = nullptr;
@@ -91,6 +94,7 @@ constexpr int ERR_EPI_WAIT = 4;
 constexpr int ERR_DRAIN_WAIT = 5;
 constexpr int ERR_TEST_WAIT = 6;
 constexpr int ERR_SK_WAIT = 7;        // a stream-K partial tile did not arrive
+constexpr int ERR_GRID_BARRIER = 8;   // the one-launch per-tensor quantiser's grid barrier
 
 // Upper bound on CTA pairs of the pair GEMM (stream-K flag array size).
 constexpr int kSkMaxPairs = 128;

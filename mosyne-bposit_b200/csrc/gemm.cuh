@@ -31,6 +31,10 @@ struct EpiParams {
   // Batched GEMM (CTA-pair kernel with TMA-store outputs only): A [batch][M][K],
   // B [batch][N][K], outputs and scales contiguous per entry.
   int batch = 1;
+  // The GEMM may read B before the kernel it depends on (programmatic
+  // dependent launch) has finished: B was final when that kernel started.
+  // The single-CTA kernel then prefetches its B tiles into L2 first thing.
+  int b_prefetch = 0;
 };
 
 enum GemmPath {

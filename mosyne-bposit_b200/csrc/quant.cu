@@ -9,6 +9,11 @@
 #include "common.cuh"
 #include "quant.cuh"
 
+// kPdlNote: the activation quantisers let a programmatic dependent launch
+// (the W8A8 GEMM that follows them) start at once.  The dependent waits
+// (griddepcontrol.wait) before it reads anything these kernels write; what it
+// may read earlier -- its weights -- was final when the quantiser started,
+// since the quantiser itself is an ordinary launch.
 namespace mb {
 namespace {
 
@@ -42,6 +47,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
                                                          float* __restrict__ scale,
                                                          const uint32_t* __restrict__ given_amax,
                                                          int amax_stride, int reverse) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
   constexpr int V = Vec<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = (reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x) * 8 + warp;
@@ -92,6 +98,7 @@ __global__ void __launch_bounds__(256) quant_row_block_kernel(
     const T* __restrict__ x, int C, int8_t* __restrict__ q, float* __restrict__ scale,
     const uint32_t* __restrict__ given_amax, int amax_stride, float* __restrict__ scalar_scale,
     int reverse) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
   constexpr int V = Vec<T>::N;
   __shared__ float red[8];
   const int row = reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
@@ -142,12 +149,23 @@ __global__ void __launch_bounds__(256) quant_row_block_kernel(
 // re-reads it, and with thousands of rows in flight the second read misses
 // L2).  NV 16-byte vectors per thread cover rows of up to 256 * NV * V
 // elements; each of the NV loads is one 4 KiB coalesced block read.
-template <typename T, int NV>
+//
+// PT: one scale for the whole tensor, in the same single launch.  Launched
+// cooperatively (every block resident), one block per row: each block adds
+// its row |max| to the call's slot and arrives at a grid barrier; the last
+// to arrive reads the maximum, writes the scalar scale, clears the next
+// call's slot and the arrival count, and opens the next generation, which
+// releases the others.  The state is self-resetting (graph replays work) and
+// the wait is bounded (a give-up sets the device error word).
+template <typename T, int NV, bool PT>
 __global__ void __launch_bounds__(256) quant_row_reg_kernel(const T* __restrict__ x, int C,
                                                             int8_t* __restrict__ q,
-                                                            float* __restrict__ scale) {
+                                                            float* __restrict__ scale,
+                                                            unsigned int* bar, int* err) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
   constexpr int V = Vec<T>::N;
   __shared__ float red[8];
+  __shared__ float gmax;
   const int row = blockIdx.x;
   const T* xr = x + (size_t)row * C;
   int8_t* qr = q + (size_t)row * C;
@@ -169,8 +187,40 @@ __global__ void __launch_bounds__(256) quant_row_reg_kernel(const T* __restrict_
   __syncthreads();
   m = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
             fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+  if (PT) {
+    if (threadIdx.x == 0) {
+      unsigned g;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+      unsigned int* slot = bar + 2 + (g & 1u);
+      atomicMax(slot, __float_as_uint(m));
+      __threadfence();
+      if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+        const float mx = __uint_as_float(atomicAdd(slot, 0u));
+        bar[2 + ((g + 1u) & 1u)] = 0u;             // the next call's slot starts at zero
+        bar[0] = 0u;
+        if (scale) *scale = quant_scale_from_max(mx);
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 1), "r"(g + 1u) : "memory");
+        gmax = mx;
+      } else {
+        unsigned cur = g;
+        const unsigned long long t0 = globaltimer_ns();
+        while (cur == g) {
+          __nanosleep(100);
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(bar + 1) : "memory");
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            set_error(err, ERR_GRID_BARRIER);
+            break;
+          }
+        }
+        gmax = __uint_as_float(atomicAdd(slot, 0u));
+      }
+    }
+    __syncthreads();
+    m = gmax;
+  }
   const float s = quant_scale_from_max(m);
-  if (threadIdx.x == 0 && scale) scale[row] = s;
+  if (!PT && threadIdx.x == 0 && scale) scale[row] = s;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int c = (j * 256 + (int)threadIdx.x) * V;
@@ -218,6 +268,7 @@ __global__ void __launch_bounds__(256) colmajor_quant_kernel(const T* __restrict
                                                              int amax_stride,
                                                              int8_t* __restrict__ q,
                                                              float* __restrict__ scale) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
   __shared__ __align__(16) int8_t tile[64][64 + 16];
   __shared__ float srow[64];
   const int m0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
@@ -326,6 +377,7 @@ __global__ void __launch_bounds__(256) colmajor_quant_vec_kernel(const T* __rest
                                                                  int8_t* __restrict__ q,
                                                                  float* __restrict__ scale,
                                                                  int reverse) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
   __shared__ uint32_t tile[64][17];
   __shared__ float srow[64];
   const unsigned nb = gridDim.x * gridDim.y;
@@ -441,7 +493,27 @@ constexpr int kBlockPerRowMax = 2048;
 
 template <typename T, int NV>
 void launch_row_reg(const void* x, int R, int C, int8_t* q, float* scale, cudaStream_t st) {
-  quant_row_reg_kernel<T, NV><<<(unsigned)R, 256, 0, st>>>(static_cast<const T*>(x), C, q, scale);
+  quant_row_reg_kernel<T, NV, false><<<(unsigned)R, 256, 0, st>>>(static_cast<const T*>(x), C, q,
+                                                                  scale, nullptr, nullptr);
+}
+
+// The one-launch per-tensor quantiser (rows held in registers, grid barrier);
+// false when the rows cannot all be resident or the launch is refused.
+template <typename T, int NV>
+bool launch_row_reg_pt(DeviceContext* ctx, const void* x, int R, int C, int8_t* q, float* scale,
+                       cudaStream_t st) {
+  auto kern = quant_row_reg_kernel<T, NV, true>;
+  if (R > resident_blocks((const void*)kern, 256, 0, ctx->num_sms)) return false;
+  const T* xx = static_cast<const T*>(x);
+  unsigned int* bar = ctx->pt_bar;
+  int* err = ctx->err;
+  void* args[] = {(void*)&xx, (void*)&C, (void*)&q, (void*)&scale, (void*)&bar, (void*)&err};
+  if (cudaLaunchCooperativeKernel((const void*)kern, dim3((unsigned)R), dim3(256), args, 0, st) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
 }
 
 // `reverse` walks the rows last to first: after a pass that streamed the
@@ -539,6 +611,17 @@ int colmajor_per_token_t(DeviceContext* ctx, const void* x, int M, int K, int8_t
 template <typename T>
 int per_tensor_t(DeviceContext* ctx, const void* t, int rows, int cols, int8_t* q, float* scale,
                  bool row_major, cudaStream_t st) {
+  constexpr int V = Vec<T>::N;
+  if (row_major && ctx->pt_bar && cols % V == 0 && aligned16<T>(t) &&
+      (reinterpret_cast<uintptr_t>(q) % V) == 0 && cols <= 256 * V * 16) {
+    const int nv = (cols + 256 * V - 1) / (256 * V);
+    const bool ok = nv <= 1   ? launch_row_reg_pt<T, 1>(ctx, t, rows, cols, q, scale, st)
+                    : nv <= 2 ? launch_row_reg_pt<T, 2>(ctx, t, rows, cols, q, scale, st)
+                    : nv <= 4 ? launch_row_reg_pt<T, 4>(ctx, t, rows, cols, q, scale, st)
+                    : nv <= 8 ? launch_row_reg_pt<T, 8>(ctx, t, rows, cols, q, scale, st)
+                              : launch_row_reg_pt<T, 16>(ctx, t, rows, cols, q, scale, st);
+    if (ok) return RC_OK;
+  }
   if (ensure_scratch(reinterpret_cast<void**>(&ctx->amax), &ctx->amax_bytes, sizeof(uint32_t)))
     return RC_ALLOC;
   cudaMemsetAsync(ctx->amax, 0, sizeof(uint32_t), st);

@@ -118,6 +118,44 @@ def test_per_tensor_quantisation(cuda_lib):
     assert np.array_equal(r["bp32"].cpu().numpy().view(np.uint32), O.encode_int_array(acc, 0, 32))
 
 
+def test_per_tensor_one_launch_graph_replays(cuda_lib):
+    """The per-tensor quantiser that finds the tensor's |max| and quantises in
+    one launch (a grid barrier whose state resets itself): a CUDA graph of the
+    per-tensor linear replayed on changing inputs gives each input's exact
+    result, with the two-pass quantiser (rows too long for one launch) run
+    between the replays."""
+    from mosyne_bposit import _api, ops
+    M, K, N = 96, 1024, 520
+    g = torch.Generator().manual_seed(17)
+    wq, ws = ops.quantize_per_channel((torch.randn(N, K, generator=g) * 0.02).cuda())
+    wq_h, ws_h = wq.cpu().numpy(), ws.cpu().numpy()
+    x_buf = torch.empty(M, K, device="cuda")
+    xs = [torch.randn(M, K, generator=g) * (1 + 3 * i) for i in range(3)]
+    x_buf.copy_(xs[0].cuda())
+    ops.linear_w8a8(x_buf, wq, ws, out_dtype=torch.float32, bp32=True, per_tensor=True)  # warm-up
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream), torch.cuda.graph(graph, stream=stream):
+        r = ops.linear_w8a8(x_buf, wq, ws, out_dtype=torch.float32, bp32=True, per_tensor=True)
+    torch.cuda.synchronize()
+    for i, x in enumerate(xs):
+        x_buf.copy_(x.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        xq, xsc = O.quant_per_tensor(x.numpy())
+        acc = O.gemm_exact(xq, wq_h.T)
+        y_ref = O.dequant(acc, np.full(M, xsc, np.float32), ws_h)
+        assert np.array_equal(r["y"].cpu().numpy().view(np.uint32), y_ref.view(np.uint32)), i
+        assert np.array_equal(r["bp32"].cpu().numpy().view(np.uint32), O.encode_int_array(acc, 0, 32))
+        big = torch.randn(300, 20000, generator=g)
+        q_b, _ = ops.quantize_per_tensor(big.cuda())
+        assert np.array_equal(q_b.cpu().numpy(), O.quant_per_tensor(big.numpy())[0])
+    del graph
+    assert _api.last_error() == 0
+
+
 def test_per_token_quantiser_layouts(cuda_lib):
     from mosyne_bposit import ops
     # row lengths for every register-resident variant (1, 2, 4, 8, 16 vectors
