@@ -268,6 +268,16 @@ int mosyne_bposit_ffn_swiglu_w8a8(const void* x, int x_dtype, int M, int D,
 int mosyne_bposit_bposit8_to_int8(const uint8_t* in, size_t n, int8_t* out,
                                   mosyne_stream_t stream);
 
+/* kernels/test_mera_isometry_imma.cu:224-352 (the bposit8 IMMA path) as one
+ * call: bposit8 A [M,K] and B [N,K] (K contiguous) are decoded to int8 (6
+ * fraction bits) in one launch into library scratch, then the fused GEMM
+ * writes bposit32 of acc / 2^12 (truncate, or RTNE with MOSYNE_RTNE_BP32)
+ * and/or the raw INT32 accumulator; column-major [M,N] unless
+ * MOSYNE_OUT_ROW_MAJOR.  Calls share the scratch: order them on one stream. */
+int mosyne_bposit_gemm_bposit8(const uint8_t* A, const uint8_t* B, int M, int N, int K,
+                               uint32_t* out_bp32, int32_t* out_i32, int flags,
+                               mosyne_stream_t stream);
+
 /* kernels/bposit16_reference.py:485-503 (exact value of each binary float):
  * x of dtype MOSYNE_DT_F32 or MOSYNE_DT_F64 -> bposit16 (nbits 16, uint16
  * out) or bposit32 (nbits 32, uint32 out). */

@@ -36,9 +36,28 @@ __device__ __forceinline__ uint32_t decode4(const uint32_t* lut, uint32_t lane4,
   return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 
+// One stretch of bytes to decode: an unaligned head and tail, 16-byte vectors
+// between them.
+struct Bp8Seg {
+  const uint8_t* in;
+  int8_t* out;
+  size_t n, head, nvec;
+};
+
+__device__ __forceinline__ void bp8_seg_ends(const Bp8Table& tab, const Bp8Seg& sg, size_t tid,
+                                             size_t stride) {
+  const size_t tail0 = sg.head + sg.nvec * 16;
+  for (size_t i = tid; i < sg.head; i += stride) sg.out[i] = tab.v[sg.in[i]];
+  for (size_t i = tail0 + tid; i < sg.n; i += stride) sg.out[i] = tab.v[sg.in[i]];
+}
+
+// Up to two stretches in one launch (the A and B operands of a bposit8 GEMM):
+// the grid strides over the vectors of both in turn.
 __global__ void __launch_bounds__(kBp8Threads) bp8_to_i8_kernel(
-    const __grid_constant__ Bp8Table tab, const uint8_t* __restrict__ in,
-    int8_t* __restrict__ out, size_t n, size_t head, size_t nvec) {
+    const __grid_constant__ Bp8Table tab, Bp8Seg s0, Bp8Seg s1) {
+  // a GEMM launched after this kernel as a programmatic dependent waits for
+  // it before reading anything; it may set itself up meanwhile
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint32_t lut[];
   for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x)
     lut[i] = (uint32_t)(uint8_t)tab.v[i >> 5];
@@ -46,30 +65,33 @@ __global__ void __launch_bounds__(kBp8Threads) bp8_to_i8_kernel(
   const uint32_t lane4 = (threadIdx.x & 31u) * 4u;
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
-  // unaligned head and tail, one byte per thread
-  const size_t tail0 = head + nvec * 16;
-  for (size_t i = tid; i < head; i += stride) out[i] = tab.v[in[i]];
-  for (size_t i = tail0 + tid; i < n; i += stride) out[i] = tab.v[in[i]];
-  const uint4* src = reinterpret_cast<const uint4*>(in + head);
-  uint4* dst = reinterpret_cast<uint4*>(out + head);
+  bp8_seg_ends(tab, s0, tid, stride);
+  bp8_seg_ends(tab, s1, tid, stride);
+  const size_t nv = s0.nvec + s1.nvec;
   constexpr int U = 4;                       // independent 16-byte loads in flight
-  for (size_t i0 = tid; i0 < nvec; i0 += U * stride) {
+  for (size_t i0 = tid; i0 < nv; i0 += U * stride) {
     uint4 w[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const size_t i = i0 + u * stride;
-      if (i < nvec) w[u] = __ldcs(src + i);
+      if (i < nv) {
+        const Bp8Seg& sg = i < s0.nvec ? s0 : s1;
+        const size_t j = i < s0.nvec ? i : i - s0.nvec;
+        w[u] = __ldcs(reinterpret_cast<const uint4*>(sg.in + sg.head) + j);
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const size_t i = i0 + u * stride;
-      if (i < nvec) {
+      if (i < nv) {
+        const Bp8Seg& sg = i < s0.nvec ? s0 : s1;
+        const size_t j = i < s0.nvec ? i : i - s0.nvec;
         uint4 r;
         r.x = decode4(lut, lane4, w[u].x);
         r.y = decode4(lut, lane4, w[u].y);
         r.z = decode4(lut, lane4, w[u].z);
         r.w = decode4(lut, lane4, w[u].w);
-        __stcs(dst + i, r);
+        __stcs(reinterpret_cast<uint4*>(sg.out + sg.head) + j, r);
       }
     }
   }
@@ -80,27 +102,41 @@ bool g_bp8_ready = false;
 
 }  // namespace
 
-int bp8_to_i8_run(const uint8_t* in, size_t n, int8_t* out, int num_sms, cudaStream_t st) {
+namespace {
+
+Bp8Seg bp8_seg(const uint8_t* in, size_t n, int8_t* out) {
+  // 16-byte vectors need the same alignment phase on both sides
+  const uintptr_t ai = reinterpret_cast<uintptr_t>(in), ao = reinterpret_cast<uintptr_t>(out);
+  Bp8Seg sg{in, out, n, n, 0};
+  if ((ai & 15u) == (ao & 15u)) {
+    sg.head = (16u - (ai & 15u)) & 15u;
+    if (sg.head > n) sg.head = n;
+    sg.nvec = (n - sg.head) / 16;
+  }
+  return sg;
+}
+
+}  // namespace
+
+int bp8_to_i8_pair_run(const uint8_t* in0, size_t n0, int8_t* out0, const uint8_t* in1,
+                       size_t n1, int8_t* out1, int num_sms, cudaStream_t st) {
   if (!g_bp8_ready) {                 // 256 host-side decodes, same on every device
     for (int i = 0; i < 256; ++i) g_bp8_table.v[i] = bp::bposit8_to_int8((uint32_t)i);
     g_bp8_ready = true;
   }
-  if (n == 0) return RC_OK;
-  // 16-byte vectors need the same alignment phase on both sides
-  const uintptr_t ai = reinterpret_cast<uintptr_t>(in), ao = reinterpret_cast<uintptr_t>(out);
-  size_t head = n, nvec = 0;
-  if ((ai & 15u) == (ao & 15u)) {
-    head = (16u - (ai & 15u)) & 15u;
-    if (head > n) head = n;
-    nvec = (n - head) / 16;
-  }
+  if (n0 + n1 == 0) return RC_OK;
+  const Bp8Seg s0 = bp8_seg(in0, n0, out0), s1 = bp8_seg(in1, n1, out1);
   if (ensure_smem_attr((const void*)bp8_to_i8_kernel, kBp8SmemBytes) != RC_OK) return RC_LAUNCH;
-  const size_t work = nvec ? nvec : n;
+  const size_t nv = s0.nvec + s1.nvec;
+  const size_t work = nv ? nv : n0 + n1;
   const unsigned blocks = stream_grid((const void*)bp8_to_i8_kernel, kBp8Threads, kBp8SmemBytes,
                                       num_sms, (work + kBp8Threads - 1) / kBp8Threads);
-  bp8_to_i8_kernel<<<blocks, kBp8Threads, kBp8SmemBytes, st>>>(g_bp8_table, in, out, n, head,
-                                                              nvec);
+  bp8_to_i8_kernel<<<blocks, kBp8Threads, kBp8SmemBytes, st>>>(g_bp8_table, s0, s1);
   return launch_rc();
+}
+
+int bp8_to_i8_run(const uint8_t* in, size_t n, int8_t* out, int num_sms, cudaStream_t st) {
+  return bp8_to_i8_pair_run(in, n, out, nullptr, 0, nullptr, num_sms, st);
 }
 
 }  // namespace mb

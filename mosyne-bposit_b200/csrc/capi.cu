@@ -61,6 +61,7 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.sk_ws);
   cudaFree(c.sk_flags);
   cudaFree(c.pt_bar);
+  cudaFree(c.bp8_buf);
   c = DeviceContext();
 }
 
@@ -681,6 +682,32 @@ int mosyne_bposit_bposit8_to_int8(const uint8_t* in, size_t n, int8_t* out,
   if (!ctx) return RC_NOT_INIT;
   if (n && (!in || !out)) return RC_BAD_ARG;
   return bp8_to_i8_run(in, n, out, ctx->num_sms, as_stream(stream));
+}
+
+int mosyne_bposit_gemm_bposit8(const uint8_t* A, const uint8_t* B, int M, int N, int K,
+                               uint32_t* out_bp32, int32_t* out_i32, int flags,
+                               mosyne_stream_t stream) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || (!out_bp32 && !out_i32)) return RC_BAD_ARG;
+  const size_t na = (size_t)M * K, nb = (size_t)N * K;
+  const size_t boff = (na + 255) & ~(size_t)255;
+  if (ensure_scratch(reinterpret_cast<void**>(&ctx->bp8_buf), &ctx->bp8_buf_bytes, boff + nb))
+    return RC_ALLOC;
+  cudaStream_t st = as_stream(stream);
+  int8_t* a8 = ctx->bp8_buf;
+  int8_t* b8 = ctx->bp8_buf + boff;
+  if (bp8_to_i8_pair_run(A, na, a8, B, nb, b8, ctx->num_sms, st) != RC_OK) return RC_LAUNCH;
+  EpiParams p;
+  p.M = M;
+  p.N = N;
+  p.bp32 = out_bp32;
+  p.i32 = out_i32;
+  p.row_major = (flags & MOSYNE_OUT_ROW_MAJOR) ? 1 : 0;
+  p.rtne32 = (flags & MOSYNE_RTNE_BP32) ? 1 : 0;
+  p.bp_shift = 12;                 // two operands with 6 fraction bits each
+  const int rc = gemm_i8_run(a8, b8, K, p, ctx, st);
+  return rc == RC_BAD_ARG ? RC_BAD_ARG : (rc ? RC_GEMM : RC_OK);
 }
 
 int mosyne_bposit_float_to_bposit(const void* x, int dtype, size_t n, void* out, int nbits,

@@ -31,6 +31,9 @@ struct DeviceContext {
   // grid barrier of the one-launch per-tensor quantiser: [0] arrivals,
   // [1] generation, [2 + (generation & 1)] that call's |max| (fp32 bits)
   unsigned int* pt_bar = nullptr;
+  // decoded int8 operands of the bposit8 GEMM (A, then B at a 256-byte boundary)
+  int8_t* bp8_buf = nullptr;
+  size_t bp8_buf_bytes = 0;
   // SwiGLU FFN intermediates: activation [M,F] fp32, its int8 codes, scales
   // and row maxima
   float* ffn_act = nullptr;

@@ -84,6 +84,7 @@ _SIGS = {
     "mosyne_bposit_bp16_to_quire": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit_int32_to_bp32": (_I, [_P, _SZ, _I, _P, _I, _P]),
     "mosyne_bposit_bposit8_to_int8": (_I, [_P, _SZ, _P, _P]),
+    "mosyne_bposit_gemm_bposit8": (_I, [_P, _P, _I, _I, _I, _P, _P, _I, _P]),
     "mosyne_bposit_ffn_swiglu_w8a8": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I, _P]),
     "mosyne_bposit_float_to_bposit": (_I, [_P, _I, _SZ, _P, _I, _I, _P]),
     "mosyne_bposit_epilogue_i32": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
@@ -372,6 +373,13 @@ def ffn_swiglu_w8a8_dev(x: int, x_dtype: int, M: int, D: int, w_gu_i8: int, w_gu
     _check(lib.mosyne_bposit_ffn_swiglu_w8a8(x, x_dtype, M, D, w_gu_i8, w_gu_scale, F, w_down_i8,
                                              w_down_scale, y, y_dtype, act, 0, stream),
            "mosyne_bposit_ffn_swiglu_w8a8")
+
+
+def gemm_bposit8_dev(A: int, B: int, M: int, N: int, K: int, *, out_bp32: int = 0,
+                     out_i32: int = 0, flags: int = 0, stream: int = 0) -> None:
+    lib = _ensure_library()
+    _check(lib.mosyne_bposit_gemm_bposit8(A, B, M, N, K, out_bp32, out_i32, flags, stream),
+           "mosyne_bposit_gemm_bposit8")
 
 
 def bposit8_to_int8_dev(x: int, n: int, out: int, *, stream: int = 0) -> None:

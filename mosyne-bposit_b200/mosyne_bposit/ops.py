@@ -391,9 +391,24 @@ def gemm_bposit8(A: torch.Tensor, B: torch.Tensor, *, bp32: bool = True, i32: bo
     tensors, kernels/test_mera_isometry_imma.cu:224-352): ``A [M,K]`` and
     ``B [N,K]`` bposit8 codes are decoded to int8 with 6 fraction bits, the
     exact INT32 GEMM runs on the tensor cores and the epilogue encodes
-    ``acc / 2^12`` to bposit32 (``i32`` returns the raw accumulator)."""
-    return gemm_i8(bposit8_to_int8(A), bposit8_to_int8(B), bp32=bp32, i32=i32, rtne32=rtne32,
-                   row_major=row_major, scale_shift=12)
+    ``acc / 2^12`` to bposit32 (``i32`` returns the raw accumulator).  Both
+    operands are decoded in one launch into library scratch."""
+    _need_cuda(A, B)
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)} vs B {tuple(B.shape)}")
+    A = A.contiguous()
+    B = B.contiguous()
+    M, K = A.shape
+    N = B.shape[0]
+    res = {}
+    if bp32:
+        res["bp32"] = _out((M, N), torch.int32, A.device, row_major)
+    if i32:
+        res["i32"] = _out((M, N), torch.int32, A.device, row_major)
+    flags = (_api.RTNE_BP32 if rtne32 else 0) | (_api.OUT_ROW_MAJOR if row_major else 0)
+    _api.gemm_bposit8_dev(A.data_ptr(), B.data_ptr(), M, N, K, out_bp32=_ptr(res.get("bp32")),
+                          out_i32=_ptr(res.get("i32")), flags=flags, stream=_stream(A))
+    return res
 
 
 def float_to_bposit(x: torch.Tensor, nbits: int = 16, *, rtne: bool = False) -> torch.Tensor:

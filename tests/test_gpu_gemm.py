@@ -246,15 +246,20 @@ def test_gemm_bposit8_in_bposit32_out(cuda_lib):
     the reference's bposit8 IMMA pipeline, against the oracle."""
     from mosyne_bposit import _api, ops
     g = torch.Generator(device="cpu").manual_seed(88)
-    for M, N, K in ((512, 768, 1024), (37, 50, 64)):
+    # (both operands decoded in one launch: whole 16-byte vectors, ragged
+    # sizes with unaligned tails, K not a multiple of 16 -> CUDA-core GEMM)
+    for M, N, K, rm in ((512, 768, 1024, False), (37, 50, 64, False), (300, 257, 2000, True),
+                        (129, 65, 72, False), (64, 96, 40, True)):
         A = torch.randint(0, 256, (M, K), generator=g, dtype=torch.int32).to(torch.uint8)
         B = torch.randint(0, 256, (N, K), generator=g, dtype=torch.int32).to(torch.uint8)
-        r = ops.gemm_bposit8(A.cuda(), B.cuda(), i32=True)
+        r = ops.gemm_bposit8(A.cuda(), B.cuda(), i32=True, row_major=rm)
         a8 = O.bposit8_to_int8_array(A.numpy())
         b8 = O.bposit8_to_int8_array(B.numpy())
         acc = O.gemm_exact(a8, b8.T)
-        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc)
+        assert np.array_equal(_np(r["i32"]).astype(np.int64), acc), (M, N, K)
         assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 12, 32))
+        rt = ops.gemm_bposit8(A.cuda(), B.cuda(), rtne32=True)
+        assert np.array_equal(_np(rt["bp32"], np.uint32), O.encode_int_array(acc, 12, 32, "rtne"))
     assert _api.last_error() == 0
 
 
