@@ -42,11 +42,13 @@ __device__ __forceinline__ void q_accumulate_bp16(quire256& acc, uint32_t code) 
 // regime's sum is an ordinary integer sum of V.  Each thread keeps one int32
 // sum per regime k = -12 .. 14 in its own shared-memory column (exact for
 // 4096 values; folded into the 256-bit quire every 2048 values and at the
-// end), the decode is branch-free and the same for every code.  Regimes
-// k < -12 lie below 2^-96 and add nothing, as in the per-value conversion
-// (which truncates there); for k = -12 and -11 every V is a multiple of the
-// 2^11 / 2^3 the fold divides out, so the sum stays exact.
-constexpr int kGroups = 27;
+// end), the decode is branch-free and the same for every code: zero, NaR and
+// regimes k < -12 (below 2^-96, adding nothing, as in the per-value
+// conversion, which truncates there) go to an extra bin that is never folded,
+// so every code takes one unconditional shared atomic.  For k = -12 and -11
+// every V is a multiple of the 2^11 / 2^3 the fold divides out, so the sum
+// stays exact.
+constexpr int kGroups = 28;          // bin 0: zero, NaR and regimes below -12 (dropped)
 constexpr int kGroupLow = -12;
 constexpr int kFoldIters = 256;                          // x 8 codes per iteration
 
@@ -58,18 +60,21 @@ __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   const uint32_t z = y << ((rs + 1) & 31);
   const uint32_t e = z >> 29;
   const int V = (int)(((((z >> 18) & 0x7FFu) | 0x800u)) << e);
-  const int k = (int)y < 0 ? rs - 1 : -rs;
-  if (rest != 0u && k >= kGroupLow) atomicAdd(g + (k - kGroupLow) * BS, code_sext < 0 ? -V : V);
+  const int k = (int)y < 0 ? rs - 1 : -rs;                // zero / NaR: rs = 33, k = -33
+  const int idx = max(k - kGroupLow + 1, 0);
+  const int sg = code_sext >> 31;
+  atomicAdd(g + idx * BS, (V ^ sg) - sg);
 }
 
 template <int BS>
 __device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
 #pragma unroll 1
-  for (int i = 0; i < kGroups; ++i) {
+  g[0] = 0;                                               // the dropped bin
+  for (int i = 1; i < kGroups; ++i) {
     const int s = g[i * BS];
     if (s == 0) continue;
     g[i * BS] = 0;
-    const int sh = 8 * (i + kGroupLow) + 85;              // -11 .. 197
+    const int sh = 8 * (i - 1 + kGroupLow) + 85;          // -11 .. 197
     uint64_t mag = s < 0 ? (uint64_t)(-(long long)s) : (uint64_t)s;
     int shp = sh;
     if (shp < 0) {
