@@ -469,6 +469,11 @@ def _sha256_t(t) -> str:
     return h.hexdigest()
 
 
+def _api_sm_count() -> int:
+    from mosyne_bposit import _api
+    return _api.sm_count()
+
+
 def _c5_golden():
     p = ROOT / "tests" / "golden" / "c5_hashes.json"
     if not p.exists():
@@ -565,6 +570,11 @@ def c5_workload(dist, ws, rank, steps, warmup, chunks=4):
             return D.ksplit_gemm_i8(xq_s, wq_s, bp32=True, y_dtype=torch.float32, x_scale=xs_g,
                                     w_scale=ws_g, chunks=chunks, gather=False)
         ms_k, own_k, r = timed(kstep)
+        # the same with the chunk GEMMs on every SM (no room left for NCCL)
+        ms_k_all, _, r_all = timed(lambda: D.ksplit_gemm_i8(
+            xq_s, wq_s, bp32=True, y_dtype=torch.float32, x_scale=xs_g, w_scale=ws_g,
+            chunks=chunks, gather=False, gemm_sms=1 << 30))
+        del r_all
         # the reduce-scatter alone, on buffers of the same size
         L = D.ksplit_layout(N, ws, chunks)
         src = torch.zeros((L["padded"], M), dtype=torch.int32, device=dev)
@@ -575,12 +585,14 @@ def c5_workload(dist, ws, rank, steps, warmup, chunks=4):
         kh = {k: _sha256_t(g[k].t()) for k in ("bp32", "y")} if rank == 0 else {}
         del g, r
         out["ksplit"] = {"ms_per_step": ms_k, "tpops": ops_total / ms_k / 1e9, "rank0_ms": own_k,
-                         "chunks": chunks, "reduce_scatter_ms": ms_rs,
+                         "chunks": chunks, "gemm_sms": _api_sm_count() - D.KSPLIT_NCCL_SMS,
+                         "ms_per_step_gemm_on_all_sms": ms_k_all, "reduce_scatter_ms": ms_rs,
                          "reduce_scatter_bytes_per_rank": 4 * L["padded"] * M,
                          "reduce_scatter_busbw_gbs": (ws - 1) / ws * 4 * L["padded"] * M / ms_rs / 1e6,
-                         "note": "per step: partial INT32 GEMMs of the K slice, NCCL int32 "
-                                 "reduce-scatter per chunk (overlapping the next chunk's GEMM), "
-                                 "fp32 y + bposit32 epilogue of the owned columns"}
+                         "note": "per step: partial INT32 GEMMs of the K slice on gemm_sms SMs, "
+                                 "NCCL int32 reduce-scatter per chunk on the others (overlapping "
+                                 "the next chunk's GEMM), fp32 y + bposit32 epilogue of the owned "
+                                 "columns on all SMs"}
         if rank == 0:
             out["ksplit"]["sha256"] = kh
             if golden:

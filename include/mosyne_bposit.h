@@ -113,6 +113,13 @@ const char* mosyne_bposit_version(void);
  * error as -1. */
 int mosyne_bposit_last_error(void);
 
+/* No counterpart in the reference (cuBLASLt's SM-count target plays this role
+ * there): the GEMMs of the current device launch on at most `sms` SMs from
+ * now on (0 or >= the device's count: all), leaving the others to kernels
+ * that run beside them -- e.g. the collectives of a K-split, which then
+ * overlap the next chunk's GEMM.  Per device; not thread-safe. */
+int mosyne_bposit_set_sm_count_target(int sms);
+
 /* Diagnostic: launches one bounded device-side wait that nothing satisfies;
  * it gives up after limit_ns (capped at 2 s) and sets the device error word,
  * so the next mosyne_bposit_last_error() returns -30.  Exercises the

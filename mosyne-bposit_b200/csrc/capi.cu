@@ -366,6 +366,14 @@ int mosyne_bposit_last_error(void) {
   return rc_noalloc;
 }
 
+int mosyne_bposit_set_sm_count_target(int sms) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (sms < 0) return RC_BAD_ARG;
+  ctx->sm_target = sms >= ctx->num_sms ? 0 : sms;
+  return RC_OK;
+}
+
 int mosyne_bposit_debug_wait_timeout(unsigned long long limit_ns, mosyne_stream_t stream) {
   DeviceContext* ctx = ctx_get_or_init();
   if (!ctx) return RC_NOT_INIT;

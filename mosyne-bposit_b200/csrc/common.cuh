@@ -45,6 +45,7 @@ struct DeviceContext {
   uint32_t* ffn_amax = nullptr;
   size_t ffn_amax_bytes = 0;
   bool scratch_ok = true;          // false: entry points that must not allocate
+  int sm_target = 0;               // GEMM grids use at most this many SMs (0: all)
   // stream-K partial tiles of the CTA-pair GEMM ([pair][cta][256 cols][128 rows]
   // int32) and their per-CTA ready flags (zero between launches)
   int32_t* sk_ws = nullptr;

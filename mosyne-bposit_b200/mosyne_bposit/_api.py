@@ -63,6 +63,7 @@ _SIGS = {
     # additions
     "mosyne_bposit_version": (ctypes.c_char_p, []),
     "mosyne_bposit_last_error": (_I, []),
+    "mosyne_bposit_set_sm_count_target": (_I, [_I]),
     "mosyne_bposit_debug_wait_timeout": (_I, [ctypes.c_ulonglong, _P]),
     "mosyne_bposit_gemm_i8": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P]),
     "mosyne_bposit_gemm_i8_host": (_I, [_P, _P, _I, _I, _I, _P, _P, _I]),
@@ -228,6 +229,17 @@ def shutdown() -> None:
 
 def version() -> str:
     return load_library().mosyne_bposit_version().decode()
+
+
+def set_sm_count_target(sms: int) -> None:
+    """GEMMs of the current device use at most ``sms`` SMs (0: all)."""
+    _check(_ensure_library().mosyne_bposit_set_sm_count_target(int(sms)),
+           "mosyne_bposit_set_sm_count_target")
+
+
+def sm_count() -> int:
+    import torch
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
 
 
 def last_error() -> int:

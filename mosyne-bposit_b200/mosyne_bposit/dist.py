@@ -43,6 +43,14 @@ import torch.distributed as dist
 
 MAX_EXACT_K = (2 ** 31 - 1) // (127 * 127)    # INT32 total stays exact up to this K
 MAX_EXACT_K_WIDE = (2 ** 63 - 1) // (127 * 127)
+# SMs a chunked K-split leaves to NCCL by default (its reduce-scatter kernels)
+KSPLIT_NCCL_SMS = 16
+
+
+def _all_sms(limit) -> None:
+    if limit:
+        from . import _api
+        _api.set_sm_count_target(0)
 
 
 def shard_range(total: int, world: int, rank: int) -> tuple:
@@ -207,7 +215,8 @@ def ksplit_gemm_i8(A_shard: torch.Tensor, B_shard: torch.Tensor, *, bp32: bool =
                    reduce: str = "scatter", chunks: int = 1, gather: bool = True,
                    wide: Optional[bool] = None, local_gemm: Optional[Callable] = None,
                    local_epilogue: Optional[Callable] = None,
-                   local_widen: Optional[Callable] = None) -> dict:
+                   local_widen: Optional[Callable] = None,
+                   gemm_sms: Optional[int] = None) -> dict:
     """K-split fused GEMM: ``A_shard [M,K_r]``, ``B_shard [N,K_r]`` (this
     rank's K slice), global scales ``x_scale [M]`` / ``w_scale [N]`` (or one
     value).  Exact integer partials, summed over the ranks, then the epilogue.
@@ -219,7 +228,10 @@ def ksplit_gemm_i8(A_shard: torch.Tensor, B_shard: torch.Tensor, *, bp32: bool =
     ``(n0, n1)`` ranges, in order, and the outputs have one column per owned
     column plus padding (``ksplit_layout``).  ``reduce="all"``: every rank
     returns everything.  ``res["i32"]`` / ``res["i64"]`` is the summed
-    accumulator of the columns returned."""
+    accumulator of the columns returned.  ``gemm_sms`` (CUDA library only):
+    the chunk GEMMs run on at most that many SMs, leaving the rest to NCCL so
+    a chunk's reduction overlaps the next chunk's GEMM (default: all SMs with
+    one chunk, all but ``KSPLIT_NCCL_SMS`` with more)."""
     world, rank = _world(group)
     k_sum = _total_k(A_shard.shape[1], A_shard.device, group)
     if wide is None:
@@ -230,6 +242,27 @@ def ksplit_gemm_i8(A_shard: torch.Tensor, B_shard: torch.Tensor, *, bp32: bool =
     if k_sum > MAX_EXACT_K_WIDE:
         raise ValueError(f"K={k_sum} exceeds {MAX_EXACT_K_WIDE}: INT64 sums could wrap")
     M, N = A_shard.shape[0], B_shard.shape[0]
+    limit = None
+    if local_gemm is None and A_shard.is_cuda:
+        from . import _api
+        if gemm_sms is None and max(1, chunks) > 1:
+            gemm_sms = max(2, _api.sm_count() - KSPLIT_NCCL_SMS)
+        if gemm_sms:
+            limit = gemm_sms
+            _api.set_sm_count_target(limit)
+    try:
+        return _ksplit_body(A_shard, B_shard, M, N, wide, bp32=bp32, bp16=bp16, y_dtype=y_dtype,
+                            x_scale=x_scale, w_scale=w_scale, rtne32=rtne32, rtne16=rtne16,
+                            group=group, reduce=reduce, chunks=chunks, gather=gather,
+                            local_gemm=local_gemm, local_epilogue=local_epilogue,
+                            local_widen=local_widen, world=world, rank=rank, limit=limit)
+    finally:
+        _all_sms(limit)
+
+
+def _ksplit_body(A_shard, B_shard, M, N, wide, *, bp32, bp16, y_dtype, x_scale, w_scale, rtne32,
+                 rtne16, group, reduce, chunks, gather, local_gemm, local_epilogue, local_widen,
+                 world, rank, limit):
     dt = torch.int64 if wide else torch.int32
     acc_key = "i64" if wide else "i32"
     dev = A_shard.device
@@ -250,6 +283,7 @@ def ksplit_gemm_i8(A_shard: torch.Tensor, B_shard: torch.Tensor, *, bp32: bool =
                                            async_op=True))
         for work in pending:
             work.wait()
+        _all_sms(limit)
         acc = store.t()
         res = epi(acc, w_scale=w_scale, **kw)
         res[acc_key] = acc
@@ -274,6 +308,7 @@ def ksplit_gemm_i8(A_shard: torch.Tensor, B_shard: torch.Tensor, *, bp32: bool =
                                                   group=group, async_op=True))
     for work in pending:
         work.wait()
+    _all_sms(limit)
     # this rank's columns: block `rank` of every chunk; padded columns get
     # scale 1 (their sums are zero and are dropped)
     ws_own = w_scale
