@@ -451,3 +451,22 @@ def test_gemm_batched_stream_k(cuda_lib):
         y = O.dequant(acc, xs[z].numpy(), ws[z].numpy())
         assert np.array_equal(_np(r["y"][z]).view(np.uint32), y.view(np.uint32))
 
+
+
+def test_gemm_sm_count_target(cuda_lib):
+    """With an SM-count target the GEMMs launch smaller persistent grids (the
+    K-split leaves the other SMs to NCCL); results are unchanged."""
+    from mosyne_bposit import _api, ops
+    try:
+        for target in (40, 7, 2):
+            _api.set_sm_count_target(target)
+            for (M, N, K) in ((1024, 1500, 512), (100, 700, 1024)):
+                A = _rand_i8((M, K), target + M)
+                B = _rand_i8((N, K), target + N)
+                acc = O.gemm_exact(A.numpy(), B.numpy().T)
+                r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=True, i32=True)
+                assert np.array_equal(_np(r["i32"]).astype(np.int64), acc), (target, M, N, K)
+                assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+    finally:
+        _api.set_sm_count_target(0)
+    assert _api.last_error() == 0
