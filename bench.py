@@ -238,8 +238,10 @@ def extra_workloads(steps, warmup, peaks, select=None):
       re-quantise, down GEMM (tensor-bound; torch bf16 FFN timed beside it);
     * dec: decode-like GEMMs (M = 32 / 128 rows, K up to 11008) -> bposit32,
       cuBLASLt INT8 beside (HBM-bound: the weights dominate);
+    * sq: square GEMMs 1024^3 / 2048^3 / 3072^3 -> bposit32, cuBLASLt INT8 beside;
     * bp8: the bposit8 path at 4096^3 -- decode both operands (bposit8 ->
-      int8 fixed point) and one fused GEMM whose epilogue encodes acc / 2^12.
+      int8 fixed point) in one launch and one fused GEMM whose epilogue encodes
+      acc / 2^12.
     ``select`` (a set of those names) limits the run to some of them."""
     import torch
 
@@ -349,6 +351,20 @@ def extra_workloads(steps, warmup, peaks, select=None):
                 "bytes_per_launch": M * K + N * K + M * N * 4,
                 "frac_of_hbm": (M * K + N * K + M * N * 4) / (ms / steps) / 1e6 / hbm,
                 "bound": "hbm", "outputs": "bposit32 column-major"}
+    if want("sq"):
+        # small and mid square GEMMs -> bposit32 beside cuBLASLt INT8 (INT32 out only) in
+        # the same process, inputs rotated over > 3x L2
+        from mosyne_bposit import _api
+        lib = _api.load_library()
+        for n in (1024, 2048, 3072):
+            ms, _, _ = _time_gemm(n, n, n, steps, warmup, None, 700 + n,
+                                  lambda A, B, o, st: _ours(A, B, o, st, lib))
+            lms, _, _ = _time_gemm(n, n, n, steps, warmup, None, 800 + n, _cublas_i8)
+            ops_ = 2.0 * n ** 3
+            out[f"gemm_{n}^3"] = {
+                "us_per_launch": ms / steps * 1e3, "tpops": ops_ / (ms / steps) / 1e9,
+                "cublaslt_int8_int32_out_tpops": ops_ / (lms / steps) / 1e9,
+                "vs_cublaslt": lms / ms, "outputs": "bposit32 column-major"}
     if want("bp8"):
         # bposit8 operands (uniform codes) rotated over > 3x L2
         M = N = K = 4096
@@ -367,8 +383,9 @@ def extra_workloads(steps, warmup, peaks, select=None):
         out["bposit8_gemm_4096"] = {
             "us_per_call": ms * 1e3, "tpops": 2.0 * M * N * K / ms / 1e9,
             "frac_of_int8_peak": 2.0 * M * N * K / ms / 1e9 / (2.0 * peaks["bf16"]),
-            "bound": "tensor", "launches_per_call": 3,
-            "steps": "decode A, decode B (bposit8 -> int8 x 2^6), GEMM -> bposit32 of acc / 2^12"}
+            "bound": "tensor", "launches_per_call": 2,
+            "steps": "decode A and B in one launch (bposit8 -> int8 x 2^6), GEMM -> bposit32 "
+                     "of acc / 2^12"}
         del A8, B8
     return out
 
@@ -894,7 +911,7 @@ def main():
     ap.add_argument("--gemm-flags", type=lambda v: int(v, 0), default=0,
                     help="flags word passed to mosyne_bposit_gemm_i8 with --only-gemm "
                          "(e.g. 0x100000 * (1 + cut) pins the last-wave cut)")
-    ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,dec,bp8|all",
+    ap.add_argument("--workloads", default=None, metavar="c1,c2,qkt,ffn,dec,sq,bp8|all",
                     help="run only these secondary workloads and print them (for profilers)")
     ap.add_argument("--only-c5", action="store_true",
                     help="run only the C5 16384x8192x28672 workload (N-shard, K-split, hashes)")
