@@ -498,6 +498,40 @@ def _c5_golden():
     return json.loads(p.read_text())["rows"].get("16384")
 
 
+def c2_determinism(dist, ws, rank, runs=5):
+    """The determinism headline on every rank's GPU: the exact quire sum of
+    the headline's 65,536 bposit16 codes (tests/golden/headline_codes.npy),
+    ``runs`` times per GPU; every (GPU, run) bit pattern is gathered and
+    compared, and with the published quire word and bposit16 code
+    (tests/golden/headline.json)."""
+    import numpy as np
+    import torch
+
+    from mosyne_bposit import ops
+    gdir = ROOT / "tests" / "golden"
+    codes = np.load(gdir / "headline_codes.npy")
+    h = json.loads((gdir / "headline.json").read_text())
+    x = torch.from_numpy(codes.view(np.int16).copy()).cuda()
+    words = []
+    for _ in range(runs):
+        q, b16, b32 = ops.quire_sum_bp16(x)
+        words.append(torch.cat([q.view(torch.int32), b16.to(torch.int32), b32]))
+    mine = torch.stack(words)                                   # [runs, 10] int32
+    if dist is not None:
+        allr = [torch.empty_like(mine) for _ in range(ws)]
+        dist.all_gather(allr, mine)
+        mine = torch.stack(allr)
+    pats = mine.reshape(-1, mine.shape[-1]).cpu().numpy()
+    uniq = {p.tobytes() for p in pats}
+    first = pats[0]
+    qw = [f"{int(v):016x}" for v in first[:8].view(np.uint64)]
+    b16 = int(np.uint16(first[8] & 0xFFFF))
+    return {"gpus": ws, "runs_per_gpu": runs, "patterns_seen": len(uniq),
+            "one_bit_pattern": len(uniq) == 1, "quire_words": qw, "bposit16": f"0x{b16:04x}",
+            "bposit32": f"0x{int(np.uint32(first[9])):08x}",
+            "matches_published": qw == h["quire_words"] and b16 == h["published_bp16"]}
+
+
 def c5_workload(dist, ws, rank, steps, warmup, chunks=4):
     """C5: W8A8 16384 x 8192 x 28672 with per-token activation and
     per-channel weight scales, fp32 y + bposit32 outputs (column-major), on
@@ -786,6 +820,7 @@ def run_ours(args):
     lib_ms2, _, _ = _time_gemm(M2, N2, K2, args.steps, args.warmup, None, 400 + rank, _cublas_i8)
     e2e = _e2e(M, N, K, max(3, min(args.steps, 10)), lib, dist, ws)
     c5 = c5_workload(dist, ws, rank, max(3, min(args.steps, 10)), 2)
+    c2det = c2_determinism(dist, ws, rank)
     rc = _api.last_error()
     if rc != 0:
         raise RuntimeError(f"device error word set during the C5 runs (rc={rc})")
@@ -838,6 +873,7 @@ def run_ours(args):
         line["c5_tpops"] = {"one_gpu": c5["nshard"]["tpops"]}
     line["c5_bit_identical_to_oracle"] = {k: c5[k].get("bit_identical_to_oracle")
                                           for k in ("nshard", "ksplit") if k in c5}
+    line["c2_determinism_every_gpu"] = c2det
     line["e2e"] = e2e
     if ws == 1:
         line["workloads"].update(extra_workloads(args.steps, args.warmup, peaks))

@@ -6,6 +6,7 @@
 // always leave here K-contiguous ([M,K] row-major), the operand layout the
 // tensor-core GEMM's TMA loads, and every read is coalesced (the reference's
 // per-token kernel walks column-major x with stride M, libmosyne_bposit.cu:218).
+#include <atomic>
 #include "common.cuh"
 #include "quant.cuh"
 
@@ -233,6 +234,85 @@ __global__ void __launch_bounds__(256) quant_row_reg_kernel(const T* __restrict_
       else __stcs(reinterpret_cast<uint2*>(qr + c), *reinterpret_cast<uint2*>(o));
     }
   }
+}
+
+// Per-tensor quantisation of a small row-major tensor by ONE thread-block
+// cluster (the activation of a decode-sized W8A8 linear).  Each thread loads
+// its NV 16-byte vectors into registers (element vector v = j * CTAs * 1024 +
+// CTA * 1024 + thread, coalesced); the CTA maxima meet through distributed
+// shared memory behind the cluster's hardware barrier, so there is no grid
+// barrier in global memory, no spin and no second read; each CTA then
+// quantises what it holds.  The second cluster barrier keeps every CTA's
+// shared memory alive until all peers have read its maximum.
+constexpr int kPtThreads = 1024;
+constexpr int kPtMaxNv = 8;        // 1024 threads x 8 vectors: <= 64 registers a thread
+
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+               "memory");
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kPtThreads, 1) quant_pt_cluster_kernel(const T* __restrict__ x,
+                                                                        unsigned nvec,
+                                                                        int8_t* __restrict__ q,
+                                                                        float* __restrict__ scale) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
+  constexpr int V = Vec<T>::N;
+  __shared__ float red[32];
+  __shared__ float cta_max, all_max;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned stride = gridDim.x * kPtThreads;
+  const unsigned base = blockIdx.x * kPtThreads + threadIdx.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  uint4 raw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const unsigned v = base + (unsigned)j * stride;
+    raw[j] = v < nvec ? __ldcs(xv + v) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const T* e = reinterpret_cast<const T*>(&raw[j]);
+#pragma unroll
+    for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32<T>(e[i])));
+  }
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = warp_max(red[lane]);
+    if (lane == 0) cta_max = m;
+  }
+  cluster_barrier();                       // every CTA's maximum is in its shared memory
+  if (warp == 0) {
+    float v = 0.f;
+    if ((unsigned)lane < gridDim.x) {
+      uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&cta_max)), remote;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(lane));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    }
+    v = warp_max(v);
+    if (lane == 0) all_max = v;
+  }
+  __syncthreads();
+  const float s = quant_scale_from_max(all_max);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && scale) *scale = s;
+  uint8_t* qb = reinterpret_cast<uint8_t*>(q);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const unsigned v = base + (unsigned)j * stride;
+    if (v < nvec) {
+      const T* e = reinterpret_cast<const T*>(&raw[j]);
+      int8_t o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = quantize1(to_f32<T>(e[i]), s);
+      if (V == 4) __stcs(reinterpret_cast<unsigned int*>(qb + (size_t)v * V), *reinterpret_cast<unsigned int*>(o));
+      else __stcs(reinterpret_cast<uint2*>(qb + (size_t)v * V), *reinterpret_cast<uint2*>(o));
+    }
+  }
+  cluster_barrier();                       // no CTA leaves while a peer may read cta_max
 }
 
 // Column-major x [M,K] (m contiguous): per-row |max| via coalesced reads of
@@ -516,6 +596,64 @@ bool launch_row_reg_pt(DeviceContext* ctx, const void* x, int R, int C, int8_t* 
   return true;
 }
 
+// The one-cluster per-tensor quantiser: false when the tensor is too large
+// for one cluster or the cluster launch is refused (the caller falls back).
+// Cluster of 16 CTAs (non-portable size) where the device schedules it, else 8.
+template <typename T, int NV>
+bool launch_pt_cluster_nv(const void* x, unsigned nvec, int cl, int8_t* q, float* scale,
+                          cudaStream_t st) {
+  auto kern = quant_pt_cluster_kernel<T, NV>;
+  // whether the 16-CTA cluster is schedulable: asked once (every device of a
+  // process is the same part)
+  static std::atomic<int> big_ok{-1};
+  if (cl > 8 && big_ok.load() == 0) return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cl);
+  cfg.blockDim = dim3(kPtThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)cl;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cl > 8 && big_ok.load() < 0) {
+    int clusters = 0;
+    const bool ok =
+        cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1) == cudaSuccess &&
+        cudaOccupancyMaxActiveClusters(&clusters, (const void*)kern, &cfg) == cudaSuccess &&
+        clusters >= 1;
+    if (!ok) cudaGetLastError();
+    big_ok.store(ok ? 1 : 0);
+    if (!ok) return false;
+  }
+  if (cudaLaunchKernelEx(&cfg, kern, static_cast<const T*>(x), nvec, q, scale) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+
+template <typename T>
+bool launch_pt_cluster(const void* x, size_t n, int8_t* q, float* scale, cudaStream_t st) {
+  constexpr int V = Vec<T>::N;
+  if (n % V != 0 || !aligned16<T>(x) || (reinterpret_cast<uintptr_t>(q) % V) != 0) return false;
+  const size_t nvec = n / V;
+  for (int cl : {16, 8}) {
+    const size_t per = (size_t)cl * kPtThreads;
+    if (nvec > per * kPtMaxNv) continue;
+    const int nv = (int)((nvec + per - 1) / per);
+    const bool ok = nv <= 1   ? launch_pt_cluster_nv<T, 1>(x, (unsigned)nvec, cl, q, scale, st)
+                    : nv <= 2 ? launch_pt_cluster_nv<T, 2>(x, (unsigned)nvec, cl, q, scale, st)
+                    : nv <= 4 ? launch_pt_cluster_nv<T, 4>(x, (unsigned)nvec, cl, q, scale, st)
+                              : launch_pt_cluster_nv<T, 8>(x, (unsigned)nvec, cl, q, scale, st);
+    if (ok) return true;
+  }
+  return false;
+}
+
 // `reverse` walks the rows last to first: after a pass that streamed the
 // whole tensor (the per-tensor max), the rows it read last are still in L2.
 template <typename T>
@@ -612,6 +750,8 @@ template <typename T>
 int per_tensor_t(DeviceContext* ctx, const void* t, int rows, int cols, int8_t* q, float* scale,
                  bool row_major, cudaStream_t st) {
   constexpr int V = Vec<T>::N;
+  // small tensors: one cluster, no grid barrier
+  if (row_major && launch_pt_cluster<T>(t, (size_t)rows * (size_t)cols, q, scale, st)) return RC_OK;
   if (row_major && ctx->pt_bar && cols % V == 0 && aligned16<T>(t) &&
       (reinterpret_cast<uintptr_t>(q) % V) == 0 && cols <= 256 * V * 16) {
     const int nv = (cols + 256 * V - 1) / (256 * V);

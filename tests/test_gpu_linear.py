@@ -118,14 +118,36 @@ def test_per_tensor_quantisation(cuda_lib):
     assert np.array_equal(r["bp32"].cpu().numpy().view(np.uint32), O.encode_int_array(acc, 0, 32))
 
 
-def test_per_tensor_one_launch_graph_replays(cuda_lib):
-    """The per-tensor quantiser that finds the tensor's |max| and quantises in
-    one launch (a grid barrier whose state resets itself): a CUDA graph of the
-    per-tensor linear replayed on changing inputs gives each input's exact
-    result, with the two-pass quantiser (rows too long for one launch) run
-    between the replays."""
+@pytest.mark.parametrize("shape,dtype", [
+    ((1, 4), torch.float32), ((3, 1000), torch.float32),        # one cluster
+    ((128, 2048), torch.float32), ((128, 2048), torch.bfloat16),
+    ((512, 1024), torch.float32),                               # the largest one-cluster tensor
+    ((512, 1028), torch.float32), ((1000, 4096), torch.float16),  # grid-barrier launch
+    ((5, 7), torch.float32), ((3000, 20000), torch.float32),    # two-pass
+])
+def test_per_tensor_quantiser_paths(cuda_lib, shape, dtype):
+    """Every per-tensor quantiser (one cluster for small tensors, one launch
+    with a grid barrier, two passes) against the oracle, bit for bit."""
     from mosyne_bposit import _api, ops
-    M, K, N = 96, 1024, 520
+    g = torch.Generator().manual_seed(shape[0] * 7 + shape[1])
+    t = (torch.randn(*shape, generator=g) * 3).to(dtype)
+    if t.numel() > 8:
+        t.view(-1)[t.numel() // 3] = 40.0                      # one outlier sets the scale
+    ref_q, ref_s = O.quant_per_tensor(t.float().numpy())
+    q, s = ops.quantize_per_tensor(t.cuda())
+    assert np.array_equal(q.cpu().numpy(), ref_q)
+    assert s.cpu().numpy().view(np.uint32)[0] == np.float32(ref_s).view(np.uint32)
+    assert _api.last_error() == 0
+
+
+@pytest.mark.parametrize("M,K", [(96, 1024), (600, 2048)])
+def test_per_tensor_one_launch_graph_replays(cuda_lib, M, K):
+    """The one-launch per-tensor quantisers (one cluster; a grid barrier whose
+    state resets itself): a CUDA graph of the per-tensor linear replayed on
+    changing inputs gives each input's exact result, with the two-pass
+    quantiser (rows too long for one launch) run between the replays."""
+    from mosyne_bposit import _api, ops
+    N = 520
     g = torch.Generator().manual_seed(17)
     wq, ws = ops.quantize_per_channel((torch.randn(N, K, generator=g) * 0.02).cuda())
     wq_h, ws_h = wq.cpu().numpy(), ws.cpu().numpy()

@@ -41,6 +41,31 @@ def test_determinism_headline(cuda_lib, golden):
     assert abs(s - float(np.sum(vals_f.astype(np.float64)))) / abs(s) < 1e-4
 
 
+def test_determinism_headline_every_gpu(cuda_lib, golden):
+    """The headline's cross-GPU claim: five runs on EVERY visible GPU of the
+    box give one bit pattern (demo.sh:66-78 loops the headline binary over
+    the GPUs; det:233-252 is the five-run loop)."""
+    from mosyne_bposit import ops
+    h = golden("headline.json")
+    _, _, codes = O.det_headline_inputs()
+    seen = {}
+    for d in range(torch.cuda.device_count()):
+        with torch.cuda.device(d):
+            x = torch.from_numpy(codes.view(np.int16).copy()).to(f"cuda:{d}")
+            for run in range(5):
+                q, b16, b32 = ops.quire_sum_bp16(x)
+                seen[(d, run)] = (bytes(q.cpu().numpy().tobytes()),
+                                  int(b16.cpu().numpy().view(np.uint16)[0]),
+                                  int(b32.cpu().numpy().view(np.uint32)[0]))
+    assert len(seen) == 5 * torch.cuda.device_count()
+    patterns = set(seen.values())
+    assert len(patterns) == 1
+    qb, b16, b32 = patterns.pop()
+    w = np.frombuffer(qb, dtype=np.uint64)
+    assert [f"{int(x):016x}" for x in w] == h["quire_words"]
+    assert b16 == h["published_bp16"] and b32 == h["pyref_bp32"]
+
+
 @pytest.mark.parametrize("n", [1, 2, 7, 8, 9, 1000, 65536, 1_000_003])
 def test_exact_sum_sizes(cuda_lib, n):
     _, codes = O.exact_sum_inputs(n, seed=n)

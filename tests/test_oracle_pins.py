@@ -8,6 +8,7 @@ import math
 import random
 import struct
 from fractions import Fraction
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -146,6 +147,9 @@ def test_determinism_headline(golden):
     assert [f"{x:016x}" for x in w] == h["quire_words"]
     assert O.quire_to_bposit(q, 16) == h["published_bp16"] == 0x7627
     assert O.quire_to_bposit(q, 32) == h["pyref_bp32"]
+    # the committed codes bench.py runs on every GPU are the same bits
+    fixture = np.load(Path(__file__).resolve().parent / "golden" / "headline_codes.npy")
+    assert fixture.dtype == np.uint16 and np.array_equal(fixture, codes)
 
 
 def test_probe_hashes(golden):
