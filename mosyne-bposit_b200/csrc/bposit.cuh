@@ -195,6 +195,16 @@ BP_HD uint32_t shl_clamped(uint32_t a, int n) {
 #endif
 }
 
+BP_HD uint32_t shr_clamped(uint32_t a, int n) {
+#if defined(__CUDA_ARCH__)
+  uint32_t r;
+  asm("shr.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(n));
+  return r;
+#else
+  return (uint32_t)n >= 32u ? 0u : a >> n;
+#endif
+}
+
 template <int NBITS, bool RTNE>
 BP_HD uint32_t from_int32_tab(int32_t I, const I32Entry* tab) {
   constexpr int N1 = NBITS - 1;
@@ -468,6 +478,135 @@ BP_HD uint32_t sum16_trunc(uint32_t a, uint32_t b) {
   return from_int64<16>(I, -xl, false);
 }
 
+// Packed decode of a bposit16 magnitude code (0 .. 0x7FFF) as the quire
+// conversion sees it: bits 0-12 the mantissa (hidden one included), bits
+// 16-23 the exponent of its last place + 128, bits below 2^-96 dropped (the
+// longest regimes of the code space; a mantissa that loses every bit packs as
+// 0).  Magnitude 0 (zero, and NaR) packs to 0.  The ALU kernels hold the
+// 32,768 packed decodes in shared memory.
+BP_HD uint32_t dec16_pack(uint32_t mag) {
+  const Dec16 d = decode16(mag & 0x7FFFu);
+  if (d.zero || d.nar) return 0u;
+  uint32_t m = d.mant;
+  int x = d.exp2;
+  if (x < -kQuireFracBits) {
+    const int sh = -kQuireFracBits - x;
+    m = sh >= 32 ? 0u : (m >> sh);
+    x = -kQuireFracBits;
+  }
+  return m == 0u ? 0u : (m | ((uint32_t)(x + 128) << 16));
+}
+
+// The value of a packed decode as a float (exact: at most 13 significant
+// bits, exponents 2^-96 .. 2^125); packed 0 gives +0.
+BP_HD float dec16_value(uint32_t packed) {
+  const uint32_t m = packed & 0x1FFFu;
+  if (m == 0u) return 0.f;
+  const int lz = clz32(m);                                // m = 1.f * 2^(31 - lz)
+  const int e = 31 - lz + (int)(packed >> 16) - 128;      // exponent of the leading bit
+  const uint32_t f23 = (m << (lz + 1)) >> 9;              // fraction bits below it
+  const uint32_t bits = ((uint32_t)(e + 127) << 23) | f23;
+#if defined(__CUDA_ARCH__)
+  return __uint_as_float(bits);
+#else
+  float v;
+  memcpy(&v, &bits, 4);
+  return v;
+#endif
+}
+
+// The encoding of s in sum16_trunc_f32, indexed by s's biased exponent: the
+// prefix (regime and exponent bits), the shift that keeps the fraction, the
+// shift that exposes the dropped bits, and the step toward zero from a value
+// on the bposit16 grid (delta0 when s's fraction is zero, delta1 otherwise;
+// 0 where the encoding saturates, and the landing codes of the two
+// saturation edges).
+struct S16Entry {
+  uint32_t enc;     // prefix | fraction shift << 16 | remainder shift << 24
+  uint32_t step;    // delta0 | delta1 << 16
+};
+
+BP_HD S16Entry s16_table_entry(int bexp) {
+  constexpr uint32_t FMASK = 0x7FFFu;
+  const int scale = bexp - 127;
+  if (bexp == 0 || scale < -kScaleLimit) return S16Entry{1u | (32u << 16) | (32u << 24), 0u};
+  if (scale > kScaleLimit) {
+    const uint32_t d0 = scale == kScaleLimit + 1 ? FMASK - encode_field32<16>(kScaleLimit, 0xFFFFFFFFu, false) : 0u;
+    return S16Entry{FMASK | (32u << 16) | (32u << 24), d0};
+  }
+  const int k = scale >> 3;
+  const int fw = 12 - (k >= 0 ? k + 2 : 1 - k);
+  const uint32_t prefix = encode_field32<16>(scale, 0u, false);
+  const uint32_t d0 = scale == -kScaleLimit ? prefix - 1u : 1u;
+  return S16Entry{prefix | ((uint32_t)(32 - fw) << 16) | ((uint32_t)fw << 24), d0 | (1u << 16)};
+}
+
+// Truncated bposit16 of the exact sum of two values held exactly as floats,
+// each a bposit16 value as the quire holds it (0, or a magnitude in
+// [2^-96, 2^113) with at most 13 significant bits) -- sum16_trunc on the
+// floating-point pipe.  s = fa + fb rounded to nearest and its exact error e
+// (Knuth's TwoSum: s + e = fa + fb exactly, |e| <= half an ulp of s).  The
+// bposit16 values are floats with at most 13 significant bits, so a value of
+// them lies within |e| of s only if it is s itself: truncating s + e toward
+// zero gives the truncation of s, except when s is a bposit16 value and e
+// points toward zero, where it is the next magnitude below.  The encoder
+// saturates at the scale limits: below 2^-48 every value is minpos, from 2^49
+// up every value is maxpos, so the steps down from 2^-48 and from 2^49 land on
+// minpos and on the largest scale-48 code.
+BP_HD uint32_t sum16_trunc_f32(float fa, float fb, const S16Entry* tab) {
+#if defined(__CUDA_ARCH__)
+  const float s = __fadd_rn(fa, fb);
+  const float bv = __fsub_rn(s, fa);
+  const float e = __fadd_rn(__fsub_rn(fa, __fsub_rn(s, bv)), __fsub_rn(fb, bv));
+  const uint32_t sb = __float_as_uint(s);
+  const uint32_t eb = __float_as_uint(e);
+#else
+  volatile float vs = fa + fb;
+  const float s = vs;
+  volatile float vbv = s - fa;
+  const float bv = vbv;
+  volatile float va = s - bv;
+  const float av = va;
+  const float e = (fa - av) + (fb - bv);
+  uint32_t sb, eb;
+  memcpy(&sb, &s, 4);
+  memcpy(&eb, &e, 4);
+#endif
+  const uint32_t mag = sb & 0x7FFFFFFFu;
+  const S16Entry t = tab[mag >> 23];
+  const uint32_t x = mag << 9;
+  uint32_t field = (t.enc & 0xFFFFu) | shr_clamped(x, (int)((t.enc >> 16) & 0xFFu));
+  const uint32_t rest = shl_clamped(x, (int)(t.enc >> 24));
+  const bool tz = ((eb ^ sb) >> 31) != 0u && (eb << 1) != 0u;
+  const uint32_t delta = x == 0u ? (t.step & 0xFFFFu) : (t.step >> 16);
+  field -= (rest == 0u && tz) ? delta : 0u;
+  const uint32_t out = apply_sign<16>(field, (sb >> 31) != 0u);
+  return mag == 0u ? 0u : out;
+}
+
+// Magnitude code of a bposit16 code (two's complement of a negative one;
+// zero and NaR give 0).
+BP_HD uint32_t mag16(uint32_t p) {
+  return ((p >> 15) & 1u) ? ((0u - p) & 0x7FFFu) : (p & 0x7FFFu);
+}
+
+// The float a bposit16 code adds to a quire (its value, bits below 2^-96
+// dropped; zero and NaR give 0), with the code's sign.
+BP_HD float quire_value16(uint32_t code) {
+  const float v = dec16_value(dec16_pack(mag16(code)));
+  return ((code >> 15) & 1u) ? -v : v;
+}
+
+// Exact product of two decoded nonzero bposit16 values, truncated: the
+// mantissa product has at most 26 bits, so from_int64's encoding of it runs
+// in 32-bit arithmetic.
+BP_HD uint32_t mul16_trunc_dec(const Dec16& da, const Dec16& db) {
+  const uint32_t m = da.mant * db.mant;
+  const int lz = clz32(m);
+  return apply_sign<16>(encode_field32<16>(31 - lz + da.exp2 + db.exp2, (m << lz) << 1, false),
+                        da.neg != db.neg);
+}
+
 // Exact binary float (value = m * 2^(e)) -> bposit<NBITS>: the exact
 // rational the float denotes (bposit16_reference.py:485-503 given a Fraction).
 template <int NBITS>
@@ -544,16 +683,6 @@ BP_HD F32Entry f32_table_entry(int bexp) {
   const uint32_t regime = k >= 0 ? ((2u << k) - 1u) << (N1 - (k + 1)) : 1u << (N1 - rlen);
   const int fw = N1 - rlen - 3;
   return F32Entry{regime | ((uint32_t)e << fw), (uint32_t)(32 - fw) | ((uint32_t)fw << 8)};
-}
-
-BP_HD uint32_t shr_clamped(uint32_t a, int n) {
-#if defined(__CUDA_ARCH__)
-  uint32_t r;
-  asm("shr.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(n));
-  return r;
-#else
-  return (uint32_t)n >= 32u ? 0u : a >> n;
-#endif
 }
 
 template <int NBITS, bool RTNE>

@@ -54,6 +54,8 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.partials);
   cudaFree(c.ticket);
   cudaFree(c.lut);
+  cudaFree(c.dec16);
+  cudaFree(c.logdec16);
   cudaFree(c.ffn_act);
   cudaFree(c.ffn_h_i8);
   cudaFree(c.ffn_h_scale);
@@ -74,6 +76,8 @@ int init_device(int d) {
   if (cudaMalloc(&c.err, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c.ticket, sizeof(unsigned int)) != cudaSuccess ||
       cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess ||
+      cudaMalloc(&c.dec16, 32768 * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMalloc(&c.logdec16, 32768 * sizeof(uint32_t)) != cudaSuccess ||
       cudaMalloc(&c.sk_flags, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
       cudaMalloc(&c.pt_bar, 4 * sizeof(unsigned)) != cudaSuccess) {
     free_ctx(c);
@@ -84,7 +88,8 @@ int init_device(int d) {
       cudaMemset(c.sk_flags, 0, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
       cudaMemset(c.pt_bar, 0, 4 * sizeof(unsigned)) != cudaSuccess ||
       cudaMemcpy(c.lut, kBposit16Tables, sizeof(kBposit16Tables), cudaMemcpyHostToDevice) !=
-          cudaSuccess) {
+          cudaSuccess ||
+      alu_build_dec16(c.dec16, c.logdec16, c.lut + LUT_LOG2 * 65536) != RC_OK) {
     free_ctx(c);
     return -3;
   }
@@ -821,6 +826,22 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out) {
                     cudaMemcpyDeviceToHost) == cudaSuccess
              ? RC_OK
              : RC_LAUNCH;
+}
+
+int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out) {
+  DeviceContext* ctx = ctx_get_or_init();
+  if (!ctx) return RC_NOT_INIT;
+  if (op < 0 || op > 3 || !host_out) return RC_BAD_ARG;
+  unsigned long long* d = nullptr;
+  if (cudaMalloc(&d, 2 * sizeof(unsigned long long)) != cudaSuccess) return RC_ALLOC;
+  const unsigned long long init[2] = {0ull, ~0ull};
+  int rc = cudaMemcpy(d, init, sizeof(init), cudaMemcpyHostToDevice) == cudaSuccess ? RC_OK
+                                                                                    : RC_LAUNCH;
+  if (rc == RC_OK) rc = alu_check_run(ctx, op, d, 0);
+  if (rc == RC_OK && cudaMemcpy(host_out, d, sizeof(init), cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = RC_LAUNCH;
+  cudaFree(d);
+  return rc;
 }
 
 }  // extern "C"

@@ -53,6 +53,10 @@ struct DeviceContext {
   unsigned* sk_flags = nullptr;
   // bposit16 ALU tables, 65,536 x u16 each, device resident
   uint16_t* lut = nullptr;         // [MB_LUT_COUNT][65536]
+  // values (float bits) of the 32,768 bposit16 magnitude codes (the adder's
+  // table) and of the log2 table's entries for those codes (the multiplier's)
+  uint32_t* dec16 = nullptr;
+  uint32_t* logdec16 = nullptr;
 };
 
 enum LutId { LUT_LOG2 = 0, LUT_EXP2 = 1, LUT_SQRT = 2, LUT_RECIP = 3, LUT_TERM = 4, MB_LUT_COUNT = 5 };

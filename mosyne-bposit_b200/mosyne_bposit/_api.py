@@ -100,6 +100,7 @@ _SIGS = {
     "mosyne_bposit16_log2": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit16_exp2": (_I, [_P, _SZ, _P, _P]),
     "mosyne_bposit16_table_host": (_I, [_I, _P]),
+    "mosyne_bposit_debug_alu_check": (_I, [_I, _P]),
     "mosyne_bposit_linear_w8a8_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _P, _P]),
     "mosyne_bposit_debug_noalloc_wait_timeout": (_I, [ctypes.c_ulonglong, _P]),
 }
@@ -447,6 +448,18 @@ def bposit16_binary_dev(op: str, a: int, b: int, n: int, out: int, *, stream: in
     lib = _ensure_library()
     name = _ALU2[op]
     _check(getattr(lib, name)(a, b, n, out, stream), name)
+
+
+def debug_alu_check(op: str) -> tuple:
+    """Exhaustive check of the bposit16 ALU's 32-bit forms against their int64
+    forms over all 2^32 code pairs ("add", "mul_exact", "quire_sum" or "mul"):
+    returns (mismatching pairs, first mismatching pair index or None)."""
+    out = np.zeros(2, dtype=np.uint64)
+    idx = ("add", "mul_exact", "quire_sum", "mul").index(op)
+    _check(_ensure_library().mosyne_bposit_debug_alu_check(idx, out.ctypes.data),
+           "mosyne_bposit_debug_alu_check")
+    first = int(out[1])
+    return int(out[0]), (None if first == 2 ** 64 - 1 else first)
 
 
 def bposit16_table(which: str) -> np.ndarray:

@@ -81,6 +81,58 @@ size_t h_sum16_check(const uint16_t* bs, size_t nb) {
   return bad;
 }
 
+// Mismatches of the floating-point sum (bp::sum16_trunc_f32 of the quire
+// values) and of the 32-bit exact product (bp::mul16_trunc_dec) against the
+// int64 forms, over every code a paired with each b in bs and with the codes
+// next to -a and a.
+size_t h_alu32_check(const uint16_t* bs, size_t nb) {
+  bp::S16Entry st[256];
+  for (int i = 0; i < 256; ++i) st[i] = bp::s16_table_entry(i);
+  auto mul_ref = [](uint32_t a, uint32_t b) -> uint32_t {
+    const bp::Dec16 da = bp::decode16(a), db = bp::decode16(b);
+    if (da.zero || db.zero) return 0u;
+    if (da.nar || db.nar) return 0x8000u;
+    const int64_t m = (int64_t)da.mant * (int64_t)db.mant;
+    return bp::from_int64<16>((da.neg != db.neg) ? -m : m, -(da.exp2 + db.exp2), false);
+  };
+  auto mul_fast = [](uint32_t a, uint32_t b) -> uint32_t {
+    const bp::Dec16 da = bp::decode16(a), db = bp::decode16(b);
+    if (da.zero || db.zero) return 0u;
+    if (da.nar || db.nar) return 0x8000u;
+    return bp::mul16_trunc_dec(da, db);
+  };
+  size_t bad = 0;
+  auto one = [&](uint32_t a, uint32_t b) {
+    if (bp::sum16_trunc_f32(bp::quire_value16(a), bp::quire_value16(b), st) != bp::sum16_trunc(a, b))
+      ++bad;
+    if ((mul_fast(a, b) & 0xFFFFu) != (mul_ref(a, b) & 0xFFFFu)) ++bad;
+  };
+  for (uint32_t a = 0; a < 65536; ++a) {
+    for (size_t j = 0; j < nb; ++j) one(a, bs[j]);
+    const uint32_t na = (0u - a) & 0xFFFFu;
+    for (int d = -3; d <= 3; ++d) {
+      one(a, (na + (uint32_t)d) & 0xFFFFu);
+      one(a, (a + (uint32_t)d) & 0xFFFFu);
+    }
+  }
+  return bad;
+}
+
+// Mismatches of the floating-point sum against the int64 sum over all 2^32
+// pairs of codes (threads when built with OpenMP).
+size_t h_sum16_f32_exhaustive() {
+  bp::S16Entry st[256];
+  for (int i = 0; i < 256; ++i) st[i] = bp::s16_table_entry(i);
+  size_t bad = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : bad)
+  for (int a = 0; a < 65536; ++a) {
+    const float fa = bp::quire_value16((uint32_t)a);
+    for (uint32_t b = 0; b < 65536; ++b)
+      if (bp::sum16_trunc_f32(fa, bp::quire_value16(b), st) != bp::sum16_trunc((uint32_t)a, b)) ++bad;
+  }
+  return bad;
+}
+
 void h_from_float_tab(const float* x, size_t n, int nbits, int rtne, uint32_t* out) {
   bp::F32Entry t16[256], t32[256];
   for (int i = 0; i < 256; ++i) {

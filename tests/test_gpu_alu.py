@@ -78,3 +78,33 @@ def test_binary_ops_random(cuda_lib):
         assert int(add[i]) == O.add16(x, y), (hex(x), hex(y))
         assert int(mex[i]) == O.mul16_exact(x, y), (hex(x), hex(y))
         assert int(mul[i]) == O.mul16(x, y, lg, ex), (hex(x), hex(y))
+
+
+@pytest.mark.parametrize("op", ["add", "mul_exact", "quire_sum", "mul"])
+def test_alu_32bit_forms_equal_int64_forms_on_every_pair(cuda_lib, op):
+    """The adder, the exact multiplier, the quire sum and the log/exp
+    multiplier run in 32-bit arithmetic; on all 2^32 pairs of codes they give
+    the codes of the int64 forms they replaced (which the oracle pins)."""
+    from mosyne_bposit import _api
+    bad, first = _api.debug_alu_check(op)
+    assert bad == 0, (op, bad, None if first is None else (hex(first >> 16), hex(first & 0xFFFF)))
+
+
+def test_alu_add_staged_and_unstaged(cuda_lib):
+    """The adder reads its decode table from shared memory on large launches
+    and through L2 on small ones: both against the oracle."""
+    from mosyne_bposit import ops
+    rng = np.random.default_rng(31)
+    for n in (1000, 148 * 16384 + 77):
+        a = rng.integers(0, 65536, n).astype(np.uint16)
+        b = rng.integers(0, 65536, n).astype(np.uint16)
+        a[:8] = [0, 0x8000, 0x7FFF, 0x8001, 1, 0xFFFF, 0x4000, 0xC000]
+        b[:8] = [0x4000, 5, 0x8001, 0x7FFF, 0xFFFF, 1, 0xC000, 0x4000]
+        out = _u(ops.bposit16_op("add", _t(a), _t(b)))
+        k = min(n, 4000)
+        want = np.array([O.add16(int(x), int(y)) for x, y in zip(a[:k], b[:k])], dtype=np.uint16)
+        assert np.array_equal(out[:k], want), n
+        tail = slice(n - 2000, n)
+        want_t = np.array([O.add16(int(x), int(y)) for x, y in zip(a[tail], b[tail])],
+                          dtype=np.uint16)
+        assert np.array_equal(out[tail], want_t), n

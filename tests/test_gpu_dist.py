@@ -1,4 +1,4 @@
-"""Multi-GPU (world size 2, NCCL, one process per GPU) tests of
+"""Multi-GPU (world size 2 and every GPU of the box, NCCL, one process per GPU) tests of
 mosyne_bposit.dist on the CUDA library: the K-split linear (global row
 maxima by all_reduce(MAX), exact INT32 partials by all_reduce(SUM)) and the
 column-parallel GEMM with all-gather must equal the one-GPU results bit for
@@ -132,16 +132,23 @@ def _worker(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
-def test_ksplit_and_nshard_on_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _worlds():
+    """2 ranks, and every GPU of the box when it has more than two."""
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return [2] + ([n] if n > 2 else [])
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_ksplit_and_nshard_multi_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = sorted(q.get(timeout=240) for _ in range(2))
+    out = sorted(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         if p.is_alive():

@@ -23,7 +23,7 @@ def hlib(tmp_path_factory):
     if not gxx:
         pytest.skip("g++ not available")
     out = tmp_path_factory.mktemp("host") / "libhost_encoders.so"
-    subprocess.run([gxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-I", str(CSRC),
+    subprocess.run([gxx, "-O2", "-std=c++17", "-fopenmp", "-shared", "-fPIC", "-I", str(CSRC),
                     str(HERE / "host_encoders.cpp"), "-o", str(out)], check=True)
     lib = ctypes.CDLL(str(out))
     return lib
@@ -161,6 +161,19 @@ def test_sum16_int64_path(hlib):
     assert hlib.h_sum16_check(_p(bs), ctypes.c_size_t(bs.size)) == 0
 
 
+def test_alu_32bit_forms(hlib):
+    """The ALU's floating-point adder (TwoSum of the exact values) and 32-bit
+    exact multiplier against the int64 forms: every code against 300 codes
+    and against the codes next to its negation and itself (the GPU test
+    covers all 2^32 pairs)."""
+    rng = np.random.default_rng(41)
+    special = [0, 0x8000, 0x0001, 0xFFFF, 0x7FFF, 0x8001, 0x4000, 0xC000, 0x0002, 0x7FFE,
+               0x0100, 0xFF00, 0x3FFF, 0x4001, 0x0003, 0x0010, 0xFFF0]
+    bs = np.array(special + list(rng.integers(0, 65536, 300 - len(special))), dtype=np.uint16)
+    hlib.h_alu32_check.restype = ctypes.c_size_t
+    assert hlib.h_alu32_check(_p(bs), ctypes.c_size_t(bs.size)) == 0
+
+
 def test_headline_sum(hlib, golden):
     _, _, codes = O.det_headline_inputs()
     w = np.empty(4, dtype=np.uint64)
@@ -174,3 +187,10 @@ def test_bposit8_to_int8_table(hlib, golden):
     out = np.zeros(256, dtype=np.int8)
     hlib.h_bp8_to_i8(_p(out))
     assert out.tolist() == golden("bposit8.json")["to_int8"]
+
+
+def test_sum16_f32_every_pair(hlib):
+    """The ALU's floating-point bposit16 sum equals the int64 sum on all 2^32
+    pairs of codes (the int64 sum is pinned to the quire path above)."""
+    hlib.h_sum16_f32_exhaustive.restype = ctypes.c_size_t
+    assert hlib.h_sum16_f32_exhaustive() == 0
