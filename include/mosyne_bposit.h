@@ -368,10 +368,13 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out);
 /* Test hook, no counterpart in the reference: runs the bposit16 ALU's 32-bit
  * forms -- op 0 the adder (mosyne_bposit16_add), 1 the exact multiplier
  * (mosyne_bposit16_mul_exact), 2 the truncated quire sum of two codes, 3 the
- * log2/exp2 multiplier (mosyne_bposit16_mul) -- and their int64 forms on every one of the 2^32
- * pairs of codes, and writes host_out[0] = the number of pairs where they
+ * log2/exp2 multiplier (mosyne_bposit16_mul) -- and their int64 forms on
+ * every one of the 2^32 pairs of codes, and writes host_out[0] = the number of pairs where they
  * differ, host_out[1] = the first such pair (a << 16 | b; ~0 when none).
- * Synchronous; allocates 16 bytes of device memory. */
+ * op 4: the GEMM epilogue's slow-path-free dequant division against the
+ * IEEE division on 2^32 pseudo-random operand pairs (host_out[1] = the first
+ * differing pair's index).  Synchronous; allocates 16 bytes of device
+ * memory. */
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out);
 
 #ifdef __cplusplus

@@ -388,6 +388,32 @@ BP_HD uint32_t from_quire(quire256 q, bool rtne) {
   return apply_sign<NBITS>(encode_field<NBITS>(msb - kQuireFracBits, win, sticky, rtne), neg);
 }
 
+// from_quire with selects instead of branches and word indexing: the
+// magnitude (two's complement of a negative quire), its leading word by a
+// select cascade, the 64 bits below the leading one taken from that word and
+// the next lower one, and the sticky OR of everything beneath -- the same
+// scale, window and sticky bit from_quire hands to encode_field, so the same
+// code.  For the element-wise kernels, which are bound by the integer pipe.
+template <int NBITS>
+BP_HD uint32_t from_quire_sel(quire256 q, bool rtne) {
+  const bool neg = (q.w[3] >> 63) != 0;
+  if (neg) q = q_neg(q);
+  const bool n3 = q.w[3] != 0, n2 = q.w[2] != 0, n1 = q.w[1] != 0;
+  const int hi = n3 ? 3 : (n2 ? 2 : (n1 ? 1 : 0));
+  const uint64_t h = n3 ? q.w[3] : (n2 ? q.w[2] : (n1 ? q.w[1] : q.w[0]));
+  const uint64_t l = n3 ? q.w[2] : (n2 ? q.w[1] : (n1 ? q.w[0] : 0ull));
+  const uint64_t below = n3 ? (q.w[1] | q.w[0]) : (n2 ? q.w[0] : 0ull);
+  const int lz = clz64(h | 1ull);            // h == 0 only for the zero quire
+  const int msb = 64 * hi + 63 - lz;
+  // the 64 bits after the leading one: h's bits below it, then l's top bits
+  const uint64_t hs = (h << lz) << 1;
+  const uint64_t win = hs | (lz == 63 ? l : (l >> (63 - lz)));
+  const uint64_t lrest = lz == 63 ? 0ull : (l << (lz + 1));
+  const bool sticky = (lrest | below) != 0ull;
+  const uint32_t r = apply_sign<NBITS>(encode_field<NBITS>(msb - kQuireFracBits, win, sticky, rtne), neg);
+  return h == 0ull ? 0u : r;
+}
+
 // bposit16 decode: value = (-1)^neg * mant * 2^exp2 (bposit16_reference.py:302-374).
 struct Dec16 {
   uint32_t mant;   // hidden one included, <= 13 bits
@@ -595,6 +621,49 @@ BP_HD uint32_t mag16(uint32_t p) {
 BP_HD float quire_value16(uint32_t code) {
   const float v = dec16_value(dec16_pack(mag16(code)));
   return ((code >> 15) & 1u) ? -v : v;
+}
+
+// Half `half` (bits 128*half .. +127, as four 32-bit words) of the quire of a
+// bposit16 code, equal to that half of quire_from_bp16(code): the
+// magnitude m * 2^sh (m < 2^13, sh = its last place + 96 in [0, 208], bits
+// below 2^-96 dropped) occupies 32-bit words sh/32 and sh/32 + 1 of the eight;
+// a negative code is the 256-bit two's complement, whose carry enters the high
+// half only when the low half of the magnitude is zero.  32-bit arithmetic
+// and selects only.
+BP_HD void quire_half_bp16(uint32_t code, int half, uint32_t w[4]) {
+  // branch-free decode of the magnitude: after the regime run (rs bits) and
+  // its terminating bit, the top three bits are the exponent and the rest the
+  // fraction, so the value is (2^12 + f12) * 2^(8k + e - 12) (fewer fraction
+  // bits read as zeros below them)
+  const uint32_t rest = mag16(code);
+  const uint32_t y = rest << 17;
+  const int rs = clz32(y ^ (y << 1)) + 1;                 // regime run length
+  const uint32_t z = shl_clamped(y, rs + 1);
+  const int k = (int)y < 0 ? rs - 1 : -rs;
+  const int x = 8 * k + (int)(z >> 29) - 12;              // exponent of the last place
+  uint32_t m = rest == 0u ? 0u : (0x1000u | ((z << 3) >> 20));
+  int sh = x + kQuireFracBits;
+  if (sh < 0) {                                           // below 2^-96: dropped
+    m = shr_clamped(m, -sh);
+    sh = 0;
+  }
+  const int wi = sh >> 5, off = sh & 31;
+  const uint32_t lo = m << off, hi = shr_clamped(m, 32 - off);
+  const int base = 4 * half;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = (base + k == wi) ? lo : ((base + k == wi + 1) ? hi : 0u);
+  if ((code & 0x8000u) && m != 0u) {
+    // carry into this half: all of it for the low half; for the high half
+    // only when the magnitude has no bit in the low half
+    const bool low_nonzero = (wi <= 3 && lo != 0u) || (wi + 1 <= 3 && hi != 0u);
+    uint32_t c = (half == 0 || !low_nonzero) ? 1u : 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t x = ~w[k];
+      w[k] = x + c;
+      c = (c != 0u && w[k] == 0u) ? 1u : 0u;
+    }
+  }
 }
 
 // Exact product of two decoded nonzero bposit16 values, truncated: the

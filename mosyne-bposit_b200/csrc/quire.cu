@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(256) quire_to_bp_kernel(const quire256* __rest
     for (int u = 0; u < kEwUnroll; ++u) {
       const size_t i = i0 + u * stride;
       if (i < n) {
-        const uint32_t r = bp::from_quire<NB>(v[u], RTNE);
+        const uint32_t r = bp::from_quire_sel<NB>(v[u], RTNE);
         if (NB == 16) static_cast<uint16_t*>(out)[i] = (uint16_t)r;
         else static_cast<uint32_t*>(out)[i] = r;
       }
@@ -292,14 +292,15 @@ __global__ void __launch_bounds__(256) bp16_to_quire_kernel(const uint16_t* __re
     for (int u = 0; u < kEwUnroll; ++u) {
       const size_t i = i0 + u * stride;
       if (i < n) {
-        const quire256 v = bp::quire_from_bp16(c[u]);
-        const uint64_t lo = half ? v.w[2] : v.w[0], hi = half ? v.w[3] : v.w[1];
+        uint32_t w[4];
+        bp::quire_half_bp16(c[u], half, w);
+        const uint4 v = make_uint4(w[0], w[1], w[2], w[3]);
         if (VEC) {
-          __stcs(reinterpret_cast<ulonglong2*>(out + i) + half, make_ulonglong2(lo, hi));
+          __stcs(reinterpret_cast<uint4*>(out + i) + half, v);
         } else {
           uint64_t* p = reinterpret_cast<uint64_t*>(out + i) + 2 * half;
-          p[0] = lo;
-          p[1] = hi;
+          p[0] = (uint64_t)v.x | ((uint64_t)v.y << 32);
+          p[1] = (uint64_t)v.z | ((uint64_t)v.w << 32);
         }
       }
     }

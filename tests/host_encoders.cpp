@@ -43,6 +43,13 @@ void h_from_quire(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* ou
   }
 }
 
+void h_from_quire_sel(const uint64_t* w, size_t n, int nbits, int rtne, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i) {
+    bp::quire256 q{{w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]}};
+    out[i] = nbits == 16 ? bp::from_quire_sel<16>(q, rtne) : bp::from_quire_sel<32>(q, rtne);
+  }
+}
+
 void h_bp16_to_quire(const uint16_t* p, size_t n, uint64_t* w) {
   for (size_t i = 0; i < n; ++i) {
     const bp::quire256 q = bp::quire_from_bp16(p[i]);
@@ -129,6 +136,22 @@ size_t h_sum16_f32_exhaustive() {
     const float fa = bp::quire_value16((uint32_t)a);
     for (uint32_t b = 0; b < 65536; ++b)
       if (bp::sum16_trunc_f32(fa, bp::quire_value16(b), st) != bp::sum16_trunc((uint32_t)a, b)) ++bad;
+  }
+  return bad;
+}
+
+// Mismatches of the two-half 32-bit bposit16 -> quire conversion against
+// quire_from_bp16 over every code.
+size_t h_quire_half_check() {
+  size_t bad = 0;
+  for (uint32_t c = 0; c < 65536; ++c) {
+    const bp::quire256 q = bp::quire_from_bp16(c);
+    for (int h = 0; h < 2; ++h) {
+      uint32_t w[4];
+      bp::quire_half_bp16(c, h, w);
+      const uint64_t lo = (uint64_t)w[0] | ((uint64_t)w[1] << 32), hi = (uint64_t)w[2] | ((uint64_t)w[3] << 32);
+      if (lo != q.w[2 * h] || hi != q.w[2 * h + 1]) ++bad;
+    }
   }
   return bad;
 }

@@ -108,3 +108,14 @@ def test_alu_add_staged_and_unstaged(cuda_lib):
         want_t = np.array([O.add16(int(x), int(y)) for x, y in zip(a[tail], b[tail])],
                           dtype=np.uint16)
         assert np.array_equal(out[tail], want_t), n
+
+
+def test_dequant_division_equals_ieee(cuda_lib):
+    """The GEMM epilogues divide (float)acc by x_scale * w_scale without a
+    slow path when both scales are in [2^-45, 2^46): that division equals
+    the IEEE one (__fdiv_rn) on 2^32 pseudo-random pairs spanning every
+    exponent of that range, with all-ones and zero significands forced."""
+    from mosyne_bposit import _api
+    bad, first = _api.debug_alu_check("dequant_div")
+    assert bad == 0, (bad, first)
+

@@ -89,6 +89,8 @@ def test_quire_encoders(hlib, golden):
         v = int.from_bytes(rng.bytes(32), "little") & ((1 << bits) - 1)
         qs.append(v if rng.integers(0, 2) else -v)
     qs += [_q for _q in (0, 1, -1, (1 << 255) - 1, -(1 << 255) + 1, 1 << 200, -(1 << 200))]
+    qs += [s * ((1 << b) + d) for b in range(0, 255, 7) for d in (-1, 0, 1) for s in (1, -1)
+           if 0 < (1 << b) + d < (1 << 255)]
     w = np.array([O.quire_to_words(q) for q in qs], dtype=np.uint64)
     for nb in (16, 32):
         for rtne in (0, 1):
@@ -97,6 +99,9 @@ def test_quire_encoders(hlib, golden):
             mode = "rtne" if rtne else "truncate"
             exp = np.array([O.quire_to_bposit(q, nb, mode) for q in qs], dtype=np.uint32)
             assert np.array_equal(out, exp), (nb, mode)
+            sel = np.empty(len(qs), dtype=np.uint32)      # the element-wise kernels' form
+            hlib.h_from_quire_sel(_p(w), ctypes.c_size_t(len(qs)), nb, rtne, _p(sel))
+            assert np.array_equal(sel, exp), (nb, mode)
 
 
 def test_bp16_decode_all_codes(hlib):
@@ -194,3 +199,12 @@ def test_sum16_f32_every_pair(hlib):
     pairs of codes (the int64 sum is pinned to the quire path above)."""
     hlib.h_sum16_f32_exhaustive.restype = ctypes.c_size_t
     assert hlib.h_sum16_f32_exhaustive() == 0
+
+
+def test_quire_halves_every_code(hlib):
+    """The element-wise bposit16 -> quire kernel's per-lane half (32-bit words,
+    two's complement carried across the halves) equals quire_from_bp16 on
+    every code."""
+    hlib.h_quire_half_check.restype = ctypes.c_size_t
+    assert hlib.h_quire_half_check() == 0
+
