@@ -807,6 +807,14 @@ def run_ours(args):
     clocks = clk.summary()
     per_launch_ms = ms / args.steps
     value = ws * ops / (per_launch_ms * 1e-3) / 1e12
+    # at N > 1: the same GEMM on rank 0's GPU alone, the other GPUs idle, in this
+    # job -- the one-GPU reference of the same box for the weak-scaling ratio
+    solo_ms = None
+    if dist is not None:
+        _barrier(dist)
+        if rank == 0:
+            solo_ms, _, _ = _time_gemm(M, N, K, args.steps, args.warmup, None, 100, call)
+        _barrier(dist)
     # second shape (same method)
     n2, M2, N2, K2 = SECOND
     ms2, nsets2, _ = _time_gemm(M2, N2, K2, args.steps, args.warmup, dist, 200 + rank, call)
@@ -860,6 +868,7 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clocks,
         "ms_per_launch_by_rank": rank_ms,
+        "same_box_one_gpu_ms_per_launch": None if solo_ms is None else solo_ms / args.steps,
         # per GPU, this build against cuBLASLt INT8 (INT32 out only) on the same GPU
         "tpops_per_gpu": {"4096^3": achieved, "2048x14336x4096": v2 / ws},
         "cublaslt_int8_tpops": {"4096^3": lib_tpops, "2048x14336x4096": lib_tpops2},

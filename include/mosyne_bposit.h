@@ -373,7 +373,8 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out);
  * differ, host_out[1] = the first such pair (a << 16 | b; ~0 when none).
  * op 4: the GEMM epilogue's slow-path-free dequant division against the
  * IEEE division on 2^32 pseudo-random operand pairs (host_out[1] = the first
- * differing pair's index).  Synchronous; allocates 16 bytes of device
+ * differing pair's index); op 5: the same for the SwiGLU epilogue's
+ * x / (1 + expf(-x)) operands.  Synchronous; allocates 16 bytes of device
  * memory. */
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out);
 

@@ -182,8 +182,10 @@ namespace {
 // call's uploads never overwrite staging buffers still in use.
 struct HostPipe {
   bool ready = false;
-  cudaStream_t up = nullptr, compute = nullptr, down = nullptr;
-  cudaEvent_t uploaded[8] = {}, computed[8] = {};
+  // downloads alternate between two streams (two copy engines in flight)
+  cudaStream_t up = nullptr, compute = nullptr, down = nullptr, down2 = nullptr;
+  // [0, 8): blocks of B; [8, 12): pieces of A
+  cudaEvent_t uploaded[12] = {}, computed[12] = {};
 };
 HostPipe g_pipe[kMaxDevices];
 std::mutex g_pipe_mu;
@@ -194,9 +196,10 @@ HostPipe* host_pipe(int d) {
   if (!h.ready) {
     if (cudaStreamCreateWithFlags(&h.up, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&h.compute, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&h.down, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&h.down, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&h.down2, cudaStreamNonBlocking) != cudaSuccess)
       return nullptr;
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 12; ++i)
       if (cudaEventCreateWithFlags(&h.uploaded[i], cudaEventDisableTiming) != cudaSuccess ||
           cudaEventCreateWithFlags(&h.computed[i], cudaEventDisableTiming) != cudaSuccess)
         return nullptr;
@@ -481,36 +484,75 @@ int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, i
   // in B and their outputs are contiguous in the column-major result, so the
   // upload of block c + 1, the GEMM of block c and the download of block
   // c - 1 run at the same time (host->device and device->host on their own
-  // copy engines).  A goes up first, whole.
+  // copy engines).  The first block is also cut along M, so its first piece
+  // needs only a quarter of A: the downloads, which bound the call, start
+  // after A's first piece and B's first block instead of after all of A.  A
+  // piece's outputs sit contiguously in device scratch ([channels][piece
+  // rows]) and come down with one strided copy into the host result.
   const int nblk = N >= 8 * 512 ? 8 : (N >= 2 * 512 ? N / 512 : 1);
   const int step = ((N + nblk - 1) / nblk + 255) / 256 * 256;
+  const int R = (M >= 4 * 512 && nblk > 1) ? 4 : 1;
+  const int mstep = ((M + R - 1) / R + 127) / 128 * 128;
   const int gflags = flags & ~(MOSYNE_XS_SCALAR | MOSYNE_WS_SCALAR);
-  if (cudaMemcpyAsync(dA, A, mk, cudaMemcpyHostToDevice, hp->up) != cudaSuccess) return RC_LAUNCH;
+  const int nc0 = N < step ? N : step;
+  auto up = [&](void* dst, const void* src, size_t bytes, cudaEvent_t ev) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, hp->up) == cudaSuccess &&
+           cudaEventRecord(ev, hp->up) == cudaSuccess;
+  };
+  int ndown = 0;
+  auto down = [&](int m0, int mc, int n0, int nc, size_t doff, cudaEvent_t ev) {
+    cudaStream_t ds = (ndown++ & 1) ? hp->down2 : hp->down;
+    if (cudaEventRecord(ev, hp->compute) != cudaSuccess ||
+        cudaStreamWaitEvent(ds, ev, 0) != cudaSuccess)
+      return false;
+    const size_t hoff = (size_t)n0 * M + m0;
+    if (dbp && cudaMemcpy2DAsync(out_bp32 + hoff, (size_t)M * 4, dbp + doff, (size_t)mc * 4,
+                                 (size_t)mc * 4, (size_t)nc, cudaMemcpyDeviceToHost,
+                                 ds) != cudaSuccess)
+      return false;
+    if (di && cudaMemcpy2DAsync(out_i32 + hoff, (size_t)M * 4, di + doff, (size_t)mc * 4,
+                                (size_t)mc * 4, (size_t)nc, cudaMemcpyDeviceToHost,
+                                ds) != cudaSuccess)
+      return false;
+    return true;
+  };
+  // uploads in the order they are needed: A piece 0, B block 0, the other
+  // pieces of A, the other blocks of B
+  if (!up(dA, A, (size_t)(M < mstep ? M : mstep) * K, hp->uploaded[8]) ||
+      !up(dB, B, (size_t)nc0 * K, hp->uploaded[0]))
+    return RC_LAUNCH;
+  for (int r = 1; r < R && r * mstep < M; ++r) {
+    const int m0 = r * mstep, mc = M - m0 < mstep ? M - m0 : mstep;
+    if (!up(dA + (size_t)m0 * K, A + (size_t)m0 * K, (size_t)mc * K, hp->uploaded[8 + r]))
+      return RC_LAUNCH;
+  }
   int c = 0;
   for (int n0 = 0; n0 < N; n0 += step, ++c) {
     const int nc = N - n0 < step ? N - n0 : step;
     const size_t boff = (size_t)n0 * K, ooff = (size_t)n0 * M;
-    if (cudaMemcpyAsync(dB + boff, B + boff, (size_t)nc * K, cudaMemcpyHostToDevice, hp->up) !=
-            cudaSuccess ||
-        cudaEventRecord(hp->uploaded[c], hp->up) != cudaSuccess ||
-        cudaStreamWaitEvent(hp->compute, hp->uploaded[c], 0) != cudaSuccess)
-      return RC_LAUNCH;
-    const int rc = mosyne_bposit_gemm_i8(dA, dB + boff, M, nc, K, nullptr, nullptr,
-                                         dbp ? dbp + ooff : nullptr, nullptr, nullptr,
-                                         MOSYNE_DT_F32, di ? di + ooff : nullptr, gflags,
-                                         hp->compute);
-    if (rc) return rc;
-    if (cudaEventRecord(hp->computed[c], hp->compute) != cudaSuccess ||
-        cudaStreamWaitEvent(hp->down, hp->computed[c], 0) != cudaSuccess)
-      return RC_LAUNCH;
-    if (dbp && cudaMemcpyAsync(out_bp32 + ooff, dbp + ooff, (size_t)nc * M * 4,
-                               cudaMemcpyDeviceToHost, hp->down) != cudaSuccess)
-      return RC_LAUNCH;
-    if (di && cudaMemcpyAsync(out_i32 + ooff, di + ooff, (size_t)nc * M * 4,
-                              cudaMemcpyDeviceToHost, hp->down) != cudaSuccess)
-      return RC_LAUNCH;
+    if (c > 0 && !up(dB + boff, B + boff, (size_t)nc * K, hp->uploaded[c])) return RC_LAUNCH;
+    if (cudaStreamWaitEvent(hp->compute, hp->uploaded[c], 0) != cudaSuccess) return RC_LAUNCH;
+    const int pieces = c == 0 ? R : 1;
+    for (int r = 0; r < pieces && r * mstep < M; ++r) {
+      const int m0 = pieces > 1 ? r * mstep : 0;
+      const int mc = pieces > 1 ? (M - m0 < mstep ? M - m0 : mstep) : M;
+      // every piece of A this GEMM reads is up (block 0: its own piece)
+      for (int q = (pieces > 1 ? r : 0); q < (pieces > 1 ? r + 1 : R); ++q)
+        if (q * mstep < M && cudaStreamWaitEvent(hp->compute, hp->uploaded[8 + q], 0) != cudaSuccess)
+          return RC_LAUNCH;
+      const size_t doff = ooff + (size_t)nc * m0;
+      const int rc = mosyne_bposit_gemm_i8(dA + (size_t)m0 * K, dB + boff, mc, nc, K, nullptr,
+                                           nullptr, dbp ? dbp + doff : nullptr, nullptr, nullptr,
+                                           MOSYNE_DT_F32, di ? di + doff : nullptr, gflags,
+                                           hp->compute);
+      if (rc) return rc;
+      if (!down(m0, mc, n0, nc, doff, hp->computed[pieces > 1 ? 8 + r : c])) return RC_LAUNCH;
+    }
   }
-  return cudaStreamSynchronize(hp->down) == cudaSuccess ? RC_OK : RC_LAUNCH;
+  return cudaStreamSynchronize(hp->down) == cudaSuccess &&
+                 cudaStreamSynchronize(hp->down2) == cudaSuccess
+             ? RC_OK
+             : RC_LAUNCH;
 }
 
 int mosyne_bposit_ffn_swiglu_w8a8(const void* x, int x_dtype, int M, int D,
@@ -831,13 +873,14 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out) {
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out) {
   DeviceContext* ctx = ctx_get_or_init();
   if (!ctx) return RC_NOT_INIT;
-  if (op < 0 || op > 4 || !host_out) return RC_BAD_ARG;
+  if (op < 0 || op > 5 || !host_out) return RC_BAD_ARG;
   unsigned long long* d = nullptr;
   if (cudaMalloc(&d, 2 * sizeof(unsigned long long)) != cudaSuccess) return RC_ALLOC;
   const unsigned long long init[2] = {0ull, ~0ull};
   int rc = cudaMemcpy(d, init, sizeof(init), cudaMemcpyHostToDevice) == cudaSuccess ? RC_OK
                                                                                     : RC_LAUNCH;
-  if (rc == RC_OK) rc = op == 4 ? div_check_run(ctx, d, 0) : alu_check_run(ctx, op, d, 0);
+  if (rc == RC_OK)
+    rc = op >= 4 ? div_check_run(ctx, d, 0, op == 5) : alu_check_run(ctx, op, d, 0);
   if (rc == RC_OK && cudaMemcpy(host_out, d, sizeof(init), cudaMemcpyDeviceToHost) != cudaSuccess)
     rc = RC_LAUNCH;
   cudaFree(d);

@@ -114,8 +114,10 @@ def test_dequant_division_equals_ieee(cuda_lib):
     """The GEMM epilogues divide (float)acc by x_scale * w_scale without a
     slow path when both scales are in [2^-45, 2^46): that division equals
     the IEEE one (__fdiv_rn) on 2^32 pseudo-random pairs spanning every
-    exponent of that range, with all-ones and zero significands forced."""
+    exponent of that range, with all-ones and zero significands forced; and
+    silu's g / (1 + expf(-g)) where its guard lets the fast divide run."""
     from mosyne_bposit import _api
-    bad, first = _api.debug_alu_check("dequant_div")
-    assert bad == 0, (bad, first)
+    for op in ("dequant_div", "silu_div"):
+        bad, first = _api.debug_alu_check(op)
+        assert bad == 0, (op, bad, first)
 

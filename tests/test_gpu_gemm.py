@@ -148,6 +148,31 @@ def test_gemm_scalar_scales(cuda_lib):
     assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32))
 
 
+@pytest.mark.parametrize("path", [2, 5])   # one-CTA tiles, CTA pairs
+def test_gemm_scales_outside_fast_divide_range(cuda_lib, path):
+    """Blocks whose scales leave [2^-45, 2^46) take the IEEE divide, the others
+    the slow-path-free one: tiny and huge scales (subnormal and infinite
+    quotients among the outputs), scattered over rows and columns, fp32 y
+    against the oracle's IEEE division bit for bit."""
+    from mosyne_bposit import ops
+    M, N, K = 300, 520, 256
+    A, B = _rand_i8((M, K), 21), _rand_i8((N, K), 22)
+    acc = O.gemm_exact(A.numpy(), B.numpy().T)
+    xs = torch.rand(M, dtype=torch.float32) * 3 + 0.01
+    ws = torch.rand(N, dtype=torch.float32) * 2 + 0.01
+    xs[::37] = 1e-20
+    xs[5] = 3e25
+    ws[::53] = 2e-19
+    ws[100:116] = 1e30
+    for row_major in (False, True):
+        r = ops.gemm_i8(A.cuda(), B.cuda(), bp32=True, y_dtype=torch.float32, x_scale=xs.cuda(),
+                        w_scale=ws.cuda(), row_major=row_major, path=path)
+        with np.errstate(over="ignore", under="ignore", divide="ignore", invalid="ignore"):
+            y = O.dequant(acc, xs.numpy(), ws.numpy())
+        assert np.array_equal(_np(r["y"]).view(np.uint32), y.view(np.uint32)), row_major
+        assert np.array_equal(_np(r["bp32"], np.uint32), O.encode_int_array(acc, 0, 32))
+
+
 def test_gemm_extreme_values(cuda_lib):
     """All -127 / +127 operands: |acc| = 127^2 K at the top of the int32
     range used, every output the same sign."""
@@ -199,11 +224,13 @@ def test_gemm_bad_args(cuda_lib):
     assert _api.last_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 3000, 256), (64, 200, 512), (1024, 4096, 128)])
+@pytest.mark.parametrize("M,N,K", [(300, 3000, 256), (64, 200, 512), (1024, 4096, 128),
+                                   (2100, 4100, 96), (4096, 1536, 64)])
 def test_gemm_host_buffers(cuda_lib, M, N, K):
     """The host-buffer entry point (uploads, GEMM and downloads pipelined over
-    blocks of output channels) returns the oracle's INT32 and bposit32 codes,
-    column-major [N, M]."""
+    blocks of output channels, the first block also cut along M into pieces
+    with strided downloads; a ragged last piece and block) returns the
+    oracle's INT32 and bposit32 codes, column-major [N, M]."""
     from mosyne_bposit import _api
     A = _rand_i8((M, K), 11).numpy()
     B = _rand_i8((N, K), 12).numpy()
