@@ -272,6 +272,17 @@ def extra_workloads(steps, warmup, peaks, select=None):
             "frac_of_hbm": nbytes / ms / 1e6 / hbm, "bound": "hbm",
             "outputs": "fp32 y + bposit32, row-major", "weight_copies": nw,
             "timing": "CUDA-graph replay of the calls"}
+
+        def c1_tok():
+            wq, sc = ws[it[0] % nw]
+            it[0] += 1
+            ops.linear_w8a8(x, wq, sc, out_dtype=torch.float32, bp32=True)
+        ms = _events_ms(c1_tok, steps, warmup, graph=True)
+        out["linear_c1_128x2048x11008_per_token"] = {
+            "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "achieved_gbs": nbytes / ms / 1e6,
+            "frac_of_hbm": nbytes / ms / 1e6 / hbm, "bound": "hbm",
+            "outputs": "fp32 y + bposit32, row-major", "weight_copies": nw,
+            "timing": "CUDA-graph replay of the calls"}
         del ws
     if want("c2"):
         # 2^24 codes (32 MiB) of the headline distribution: magnitudes 2^U,
