@@ -374,7 +374,9 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out);
  * op 4: the GEMM epilogue's slow-path-free dequant division against the
  * IEEE division on 2^32 pseudo-random operand pairs (host_out[1] = the first
  * differing pair's index); op 5: the same for the SwiGLU epilogue's
- * x / (1 + expf(-x)) operands.  Synchronous; allocates 16 bytes of device
+ * x / (1 + expf(-x)) operands; op 6: that division's reciprocal step against
+ * the correctly rounded reciprocal on every normal divisor in [2^-110, 2^111)
+ * (host_out[1] = the bits of the first differing one).  Synchronous; allocates 16 bytes of device
  * memory. */
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out);
 

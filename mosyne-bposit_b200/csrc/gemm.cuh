@@ -74,9 +74,10 @@ int gemm_i8_batched_fused(const int8_t* A, const int8_t* B, int K, const EpiPara
 int debug_wait_run(unsigned long long limit_ns, DeviceContext* ctx, cudaStream_t st);
 
 // The epilogue's slow-path-free division against __fdiv_rn on 2^32
-// pseudo-random operand pairs of the dequant (or, `silu`, of silu's divide):
-// res[0] += mismatches, res[1] = min(first index).
-int div_check_run(DeviceContext* ctx, unsigned long long* res, cudaStream_t st, bool silu);
+// pseudo-random operand pairs of the dequant (which 0) or of silu's divide
+// (1), or its reciprocal step against __frcp_rn on every normal divisor in
+// [2^-110, 2^111) (2): res[0] += mismatches, res[1] = min(first index or bits).
+int div_check_run(DeviceContext* ctx, unsigned long long* res, cudaStream_t st, int which);
 
 // Error word of the allocation-free entry point on the current device: read
 // and cleared; RC_DEVICE_TIMEOUT when a bounded wait there gave up.

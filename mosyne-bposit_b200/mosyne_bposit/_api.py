@@ -454,10 +454,12 @@ def debug_alu_check(op: str) -> tuple:
     """Exhaustive check of the bposit16 ALU's 32-bit forms against their int64
     forms over all 2^32 code pairs ("add", "mul_exact", "quire_sum" or "mul"),
     or the GEMM epilogues' divisions against the IEEE division on 2^32
-    pseudo-random operand pairs ("dequant_div", "silu_div"):
+    pseudo-random operand pairs ("dequant_div", "silu_div"), and that divide's
+    reciprocal step on every normal divisor in its range ("div_reciprocal"):
     returns (mismatching pairs, first mismatching pair index or None)."""
     out = np.zeros(2, dtype=np.uint64)
-    idx = ("add", "mul_exact", "quire_sum", "mul", "dequant_div", "silu_div").index(op)
+    idx = ("add", "mul_exact", "quire_sum", "mul", "dequant_div", "silu_div",
+           "div_reciprocal").index(op)
     _check(_ensure_library().mosyne_bposit_debug_alu_check(idx, out.ctypes.data),
            "mosyne_bposit_debug_alu_check")
     first = int(out[1])

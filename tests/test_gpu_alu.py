@@ -115,9 +115,11 @@ def test_dequant_division_equals_ieee(cuda_lib):
     slow path when both scales are in [2^-45, 2^46): that division equals
     the IEEE one (__fdiv_rn) on 2^32 pseudo-random pairs spanning every
     exponent of that range, with all-ones and zero significands forced; and
-    silu's g / (1 + expf(-g)) where its guard lets the fast divide run."""
+    silu's g / (1 + expf(-g)) where its guard lets the fast divide run; and
+    its reciprocal step is the correctly rounded reciprocal for every normal
+    divisor in [2^-110, 2^111), the premise of the correction theorem."""
     from mosyne_bposit import _api
-    for op in ("dequant_div", "silu_div"):
+    for op in ("div_reciprocal", "dequant_div", "silu_div"):
         bad, first = _api.debug_alu_check(op)
         assert bad == 0, (op, bad, first)
 
