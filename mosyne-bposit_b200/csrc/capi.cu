@@ -39,6 +39,9 @@ struct HostStage {
   size_t bytes[6] = {};
 };
 HostStage g_stage[kMaxDevices];
+// The host-buffer entry points share a device's staging buffers: one call at
+// a time per device (each returns only after its last copy).
+std::mutex g_stage_mu[kMaxDevices];
 
 int current_device() {
   int d = -1;
@@ -335,6 +338,8 @@ int mosyne_bposit_linear_w8a8_host(const float* host_x, int M, int K, const floa
   }
   if (M <= 0 || K <= 0 || N <= 0 || !host_x || !host_w || !host_y) return RC_BAD_ARG;
   const int d = current_device();
+  if (d < 0) return RC_NOT_INIT;
+  std::lock_guard<std::mutex> stage_lock(g_stage_mu[d]);
   float* dx = static_cast<float*>(stage_buf(d, 0, (size_t)M * K * sizeof(float)));
   float* dw = static_cast<float*>(stage_buf(d, 1, (size_t)K * N * sizeof(float)));
   float* dy = static_cast<float*>(stage_buf(d, 2, (size_t)M * N * sizeof(float)));
@@ -472,6 +477,7 @@ int mosyne_bposit_gemm_i8_host(const int8_t* A, const int8_t* B, int M, int N, i
   if (!ctx) return RC_NOT_INIT;
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return RC_BAD_ARG;
   const int d = ctx->device;
+  std::lock_guard<std::mutex> stage_lock(g_stage_mu[d]);
   const size_t mk = (size_t)M * K, nk = (size_t)N * K, mn = (size_t)M * N;
   int8_t* dA = static_cast<int8_t*>(stage_buf(d, 0, mk));
   int8_t* dB = static_cast<int8_t*>(stage_buf(d, 1, nk));

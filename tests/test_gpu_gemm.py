@@ -243,6 +243,34 @@ def test_gemm_host_buffers(cuda_lib, M, N, K):
     assert _api.last_error() == 0
 
 
+def test_gemm_host_buffers_from_two_threads(cuda_lib):
+    """Host threads calling the host-buffer entry point at once (it shares the
+    device's staging buffers, one call at a time) each get their own exact
+    result."""
+    import threading
+    from mosyne_bposit import _api
+    cases = [(_rand_i8((300, 256), 31 + i).numpy(), _rand_i8((1500, 256), 41 + i).numpy())
+             for i in range(4)]
+    results = [None] * len(cases)
+
+    def run(i):
+        dev = torch.cuda.current_device()
+        torch.cuda.set_device(dev)
+        for _ in range(3):
+            results[i] = _api.gemm_i8_host(cases[i][0], cases[i][1], want_i32=True)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(len(cases))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for (A, B), (bp, i32) in zip(cases, results):
+        acc = O.gemm_exact(A, B.T)
+        assert np.array_equal(i32.astype(np.int64), acc)
+        assert np.array_equal(np.asarray(bp).view(np.uint32), O.encode_int_array(acc, 0, 32))
+    assert _api.last_error() == 0
+
+
 @pytest.mark.parametrize("shift", [6, 12, 31])
 def test_gemm_scale_shift(cuda_lib, shift):
     """bposit outputs of acc / 2^shift (negative scales included) on every
