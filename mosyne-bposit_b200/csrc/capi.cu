@@ -59,6 +59,7 @@ void free_ctx(DeviceContext& c) {
   cudaFree(c.lut);
   cudaFree(c.dec16);
   cudaFree(c.logdec16);
+  cudaFree(c.term_dec);
   cudaFree(c.ffn_act);
   cudaFree(c.ffn_h_i8);
   cudaFree(c.ffn_h_scale);
@@ -81,6 +82,7 @@ int init_device(int d) {
       cudaMalloc(&c.lut, sizeof(kBposit16Tables)) != cudaSuccess ||
       cudaMalloc(&c.dec16, 32768 * sizeof(uint32_t)) != cudaSuccess ||
       cudaMalloc(&c.logdec16, 32768 * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMalloc(&c.term_dec, 32768 * sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c.sk_flags, 2 * kSkMaxPairs * sizeof(unsigned)) != cudaSuccess ||
       cudaMalloc(&c.pt_bar, 4 * sizeof(unsigned)) != cudaSuccess) {
     free_ctx(c);
@@ -92,7 +94,8 @@ int init_device(int d) {
       cudaMemset(c.pt_bar, 0, 4 * sizeof(unsigned)) != cudaSuccess ||
       cudaMemcpy(c.lut, kBposit16Tables, sizeof(kBposit16Tables), cudaMemcpyHostToDevice) !=
           cudaSuccess ||
-      alu_build_dec16(c.dec16, c.logdec16, c.lut + LUT_LOG2 * 65536) != RC_OK) {
+      alu_build_dec16(c.dec16, c.logdec16, c.lut + LUT_LOG2 * 65536) != RC_OK ||
+      term_dec_build(c.lut + LUT_TERM * 65536, c.term_dec, &c.term_dec_ok) != RC_OK) {
     free_ctx(c);
     return -3;
   }

@@ -57,6 +57,9 @@ struct DeviceContext {
   // table) and of the log2 table's entries for those codes (the multiplier's)
   uint32_t* dec16 = nullptr;
   uint32_t* logdec16 = nullptr;
+  // the entropy's summands -term[p] pre-decoded into (group, value), p < 0x8000
+  int* term_dec = nullptr;
+  bool term_dec_ok = false;
 };
 
 enum LutId { LUT_LOG2 = 0, LUT_EXP2 = 1, LUT_SQRT = 2, LUT_RECIP = 3, LUT_TERM = 4, MB_LUT_COUNT = 5 };

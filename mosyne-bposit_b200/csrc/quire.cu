@@ -52,8 +52,8 @@ constexpr int kGroups = 28;          // bin 0: zero, NaR and regimes below -12 (
 constexpr int kGroupLow = -12;
 constexpr int kFoldIters = 256;                          // x 8 codes per iteration
 
-template <int BS>   // the block size: stride between one thread's group sums
-__device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
+// The group (regime bin) and signed within-regime value of one summand.
+__device__ __forceinline__ void group_decode(int code_sext, int& idx, int& v) {
   const uint32_t rest = (uint32_t)abs(code_sext) & 0x7FFFu;   // zero and NaR: 0
   const uint32_t y = rest << 17;
   const int rs = __clz(y ^ (y << 1)) + 1;                 // regime run length
@@ -61,9 +61,44 @@ __device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
   const uint32_t e = z >> 29;
   const int V = (int)(((((z >> 18) & 0x7FFu) | 0x800u)) << e);
   const int k = (int)y < 0 ? rs - 1 : -rs;                // zero / NaR: rs = 33, k = -33
-  const int idx = max(k - kGroupLow + 1, 0);
+  idx = max(k - kGroupLow + 1, 0);
   const int sg = code_sext >> 31;
-  atomicAdd(g + idx * BS, (V ^ sg) - sg);
+  v = (V ^ sg) - sg;
+}
+
+template <int BS>   // the block size: stride between one thread's group sums
+__device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
+  int idx, v;
+  group_decode(code_sext, idx, v);
+  atomicAdd(g + idx * BS, v);
+}
+
+// The entropy's summands pre-decoded: entry c (a probability code 0 .. 0x7FFF)
+// = the group and signed value of -term[c], packed as v << 5 | idx (0 for the
+// dropped bin); negative probability codes have the NaR term, which adds
+// nothing.  One shared load and one shared atomic per code in place of the
+// table load and the decode.
+__device__ __forceinline__ int term_dec_entry(uint32_t c, const uint16_t* term) {
+  int idx, v;
+  group_decode(-(int)(int16_t)term[c], idx, v);
+  return idx == 0 ? 0 : (int)((uint32_t)v << 5) | idx;
+}
+
+template <int BS>
+__device__ __forceinline__ void group_accumulate_dec(int* g, uint32_t code, const int* dec) {
+  const int e = (code & 0x8000u) ? 0 : dec[code & 0x7FFFu];
+  atomicAdd(g + (e & 31) * BS, e >> 5);
+}
+
+// Also counts the negative probability codes whose term is not NaR (none in
+// the table this library generates; the staged mode relies on it).
+__global__ void term_dec_build_kernel(const uint16_t* __restrict__ term, int* __restrict__ out,
+                                      unsigned* __restrict__ bad) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < 32768u) {
+    out[c] = term_dec_entry(c, term);
+    if (term[c + 32768u] != 0x8000u) atomicAdd(bad, 1u);
+  }
 }
 
 template <int BS>
@@ -176,7 +211,11 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
         const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (MODE != SUM_PLAIN) {
+          if (MODE == SUM_TERM_SMEM) {
+            const int* dec = reinterpret_cast<const int*>(tab);
+            group_accumulate_dec<BS>(g, w[j] & 0xFFFFu, dec);
+            group_accumulate_dec<BS>(g, w[j] >> 16, dec);
+          } else if (MODE != SUM_PLAIN) {
             group_accumulate_bp16<BS>(g, summand<MODE>(w[j] & 0xFFFFu, tab));
             group_accumulate_bp16<BS>(g, summand<MODE>(w[j] >> 16, tab));
           } else {
@@ -192,8 +231,12 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
     }
     done = nv * 8;
   }
-  for (size_t i = done + tid; i < n; i += stride)
-    group_accumulate_bp16<BS>(g, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab) : (int)(int16_t)x[i]);
+  for (size_t i = done + tid; i < n; i += stride) {
+    if (MODE == SUM_TERM_SMEM)
+      group_accumulate_dec<BS>(g, x[i], reinterpret_cast<const int*>(tab));
+    else
+      group_accumulate_bp16<BS>(g, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab) : (int)(int16_t)x[i]);
+  }
   acc = fold_groups<BS>(g, acc);
 
   acc = block_reduce_q(acc, sh);
@@ -456,11 +499,29 @@ int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
   // the staged table pays once its copy (128 KiB per SM, from L2) is small
   // beside the gathers it saves
   const uint16_t* term = ctx->lut + (size_t)LUT_TERM * 65536;
-  if (n >= ((size_t)1 << 20))
-    return quire_sum_launch<SUM_TERM_SMEM, 512>(ctx, p, n, term, q_out, bp16_out, bp32_out, flags,
-                                                st, max_blocks);
+  if (n >= ((size_t)1 << 20) && ctx->term_dec_ok)   // staged: the pre-decoded summands
+    return quire_sum_launch<SUM_TERM_SMEM, 512>(ctx, p, n,
+                                                reinterpret_cast<const uint16_t*>(ctx->term_dec),
+                                                q_out, bp16_out, bp32_out, flags, st, max_blocks);
   return quire_sum_launch<SUM_TERM_L2, 256>(ctx, p, n, term, q_out, bp16_out, bp32_out, flags, st,
                                             max_blocks);
+}
+
+int term_dec_build(const uint16_t* term, int* out, bool* usable) {
+  unsigned* bad = nullptr;
+  if (cudaMalloc(&bad, sizeof(unsigned)) != cudaSuccess) return RC_ALLOC;
+  unsigned h = 0;
+  int rc = cudaMemset(bad, 0, sizeof(unsigned)) == cudaSuccess ? RC_OK : RC_LAUNCH;
+  if (rc == RC_OK) {
+    term_dec_build_kernel<<<32, 1024>>>(term, out, bad);
+    rc = (cudaGetLastError() == cudaSuccess &&
+          cudaMemcpy(&h, bad, sizeof(unsigned), cudaMemcpyDeviceToHost) == cudaSuccess)
+             ? RC_OK
+             : RC_LAUNCH;
+  }
+  cudaFree(bad);
+  *usable = rc == RC_OK && h == 0;
+  return rc;
 }
 
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,

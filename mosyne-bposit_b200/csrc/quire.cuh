@@ -12,6 +12,10 @@ int quire_sum_bp16_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_q
 int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
                              mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out,
                              int flags, cudaStream_t st, int max_blocks = 0);
+// The entropy's pre-decoded summands for the 32,768 probability codes
+// (device init; term = the entropy term table); `usable` false when a
+// negative code's term is not NaR (the staged mode then is not used).
+int term_dec_build(const uint16_t* term, int* out, bool* usable);
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
                         cudaStream_t st);
 int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void* out, int nbits,
