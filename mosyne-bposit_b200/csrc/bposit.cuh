@@ -745,6 +745,7 @@ BP_HD F32Entry f32_table_entry(int bexp) {
   constexpr int N1 = NBITS - 1;
   constexpr uint32_t FMASK = (1u << N1) - 1u;
   const int scale = bexp - 127;
+  if (bexp == 0xFF) return F32Entry{1u << N1, 32u | (32u << 8)};   // inf / NaN -> NaR
   if (bexp == 0 || scale < -kScaleLimit) return F32Entry{1u, 32u | (32u << 8)};
   if (scale > kScaleLimit) return F32Entry{FMASK, 32u | (32u << 8)};
   const int k = scale >> 3, e = scale & 7;
@@ -770,13 +771,16 @@ BP_HD uint32_t from_float_tab(float xf, const F32Entry* tab) {
   const uint32_t x = u << 9;                              // fraction, MSB-aligned
   uint32_t field = t.prefix | shr_clamped(x, (int)(t.sh & 0xFFu));
   if (RTNE) {
+    // round up when the dropped bits exceed half a place, or equal it with
+    // the kept field odd; never past maxpos (the NaR entry drops nothing)
     const uint32_t rest = shl_clamped(x, (int)(t.sh >> 8));
-    field += (rest >> 31) & (uint32_t)(((rest << 1) != 0u) | (field & 1u)) & (uint32_t)(field != FMASK);
+    field += (uint32_t)((rest > 0x80000000u - (field & 1u)) && field != FMASK);
   }
+  // a negative value is the two's complement of its magnitude's code (NaR's
+  // code is its own complement)
   const uint32_t m = (uint32_t)((int32_t)u >> 31);
   const uint32_t out = ((field ^ m) - m) & NMASK;
-  const uint32_t r = (u & 0x7FFFFFFFu) == 0u ? 0u : out;
-  return bexp == 0xFFu ? (1u << N1) : r;
+  return (u & 0x7FFFFFFFu) == 0u ? 0u : out;
 }
 
 }  // namespace bp

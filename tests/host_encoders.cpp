@@ -1,5 +1,6 @@
 // Host build of the library's encoder header (mosyne-bposit_b200/csrc/bposit.cuh)
 // for CPU tests: the same source the kernels compile, exercised without a GPU.
+#include <cstring>
 #include <cstddef>
 #include <cstdint>
 
@@ -168,6 +169,31 @@ void h_from_float_tab(const float* x, size_t n, int nbits, int rtne, uint32_t* o
     else
       out[i] = rtne ? bp::from_float_tab<32, true>(x[i], t32) : bp::from_float_tab<32, false>(x[i], t32);
   }
+}
+
+// Mismatches of the table encoder against the direct float encoder over every
+// float bit pattern, bposit16 and bposit32, truncate and RTNE (threads when
+// built with OpenMP).
+size_t h_from_float_tab_exhaustive() {
+  bp::F32Entry t16[256], t32[256];
+  for (int i = 0; i < 256; ++i) {
+    t16[i] = bp::f32_table_entry<16>(i);
+    t32[i] = bp::f32_table_entry<32>(i);
+  }
+  size_t bad = 0;
+#pragma omp parallel for schedule(dynamic, 256) reduction(+ : bad)
+  for (int hi = 0; hi < 65536; ++hi) {
+    for (uint32_t lo = 0; lo < 65536; ++lo) {
+      const uint32_t u = ((uint32_t)hi << 16) | lo;
+      float f;
+      memcpy(&f, &u, 4);
+      bad += bp::from_float_tab<16, true>(f, t16) != bp::from_float<16>(f, true);
+      bad += bp::from_float_tab<16, false>(f, t16) != bp::from_float<16>(f, false);
+      bad += bp::from_float_tab<32, true>(f, t32) != bp::from_float<32>(f, true);
+      bad += bp::from_float_tab<32, false>(f, t32) != bp::from_float<32>(f, false);
+    }
+  }
+  return bad;
 }
 
 void h_quire_sum(const uint16_t* p, size_t n, uint64_t* w) {

@@ -201,6 +201,16 @@ def test_sum16_f32_every_pair(hlib):
     assert hlib.h_sum16_f32_exhaustive() == 0
 
 
+def test_float_table_encoder_every_pattern(hlib):
+    """The kernels' table encoder (one 256-entry lookup by the float's biased
+    exponent, then shifts and the RTNE increment) equals the direct float
+    encoder on every one of the 2^32 float bit patterns, for bposit16 and
+    bposit32, truncate and RTNE (the direct encoder is pinned to the oracle in
+    test_float_encoder)."""
+    hlib.h_from_float_tab_exhaustive.restype = ctypes.c_size_t
+    assert hlib.h_from_float_tab_exhaustive() == 0
+
+
 def test_quire_halves_every_code(hlib):
     """The element-wise bposit16 -> quire kernel's per-lane half (32-bit words,
     two's complement carried across the halves) equals quire_from_bp16 on
