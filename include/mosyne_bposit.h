@@ -376,7 +376,9 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out);
  * differing pair's index); op 5: the same for the SwiGLU epilogue's
  * x / (1 + expf(-x)) operands; op 6: that division's reciprocal step against
  * the correctly rounded reciprocal on every normal divisor in [2^-110, 2^111)
- * (host_out[1] = the bits of the first differing one).  Synchronous; allocates 16 bytes of device
+ * (host_out[1] = the bits of the first differing one); op 7: the exact sum's per-code decode
+ * (regime and integer value within the regime) against the quire image of every bposit16
+ * code (host_out[1] = the first differing code).  Synchronous; allocates 16 bytes of device
  * memory. */
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out);
 

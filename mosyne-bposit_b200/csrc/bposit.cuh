@@ -467,6 +467,46 @@ BP_HD quire256 quire_from_bp16(uint32_t p) {
   return d.neg ? q_neg(q) : q;
 }
 
+// Regime-bin decode of one bposit16 code for the exact sum.  c32 holds the code
+// in its upper 16 bits (lower 16 bits zero), so the 32-bit negate is the code's
+// own two's-complement negate.  With W = 1.f scaled to an integer (2^11 + f)
+// and e the exponent, a code of regime k has value * 2^96 = (W << e) *
+// 2^(8k + 85): within one regime the value is the integer V = W << e < 2^19.
+// Returns k and the signed V.  Real codes have k = -14 .. 14; zero and NaR
+// return k = -15 (the bit at 16 stops their run of zeros there), so a caller
+// with bins for k = -15 .. 14 needs no clamp and drops k < -12 (values under
+// 2^-96, which the per-value quire conversion truncates to zero).  Branch-free:
+// the regime run is one count of leading zeros of the bits after the sign,
+// inverted when they are ones.  V is formed as a float with exponent field
+// e + 138 and fraction f (exactly V), then times the code's sign plus
+// 1.5 * 2^23 in one fused multiply-add, exact for |V| < 2^22 (the sum's unit
+// is 1), whose bits less those of 1.5 * 2^23 are the integer +-V: the
+// multiply-add pipe does what took five integer operations (the exponent,
+// the fraction with its hidden bit, the shift, the conditional negate).
+BP_HD void sum_bin16(int32_t c32, int& k, int& v) {
+  const uint32_t a = c32 < 0 ? 0u - (uint32_t)c32 : (uint32_t)c32;   // NaR: 0x80000000
+  const uint32_t xs = (uint32_t)((int32_t)(a << 1) >> 31);  // all ones: a run of ones (k >= 0)
+  // run length - 1 (bit 17 caps zero and NaR at 14); the lowest bit of xs is
+  // below that cap and does not matter
+  const int m1 = clz32(((a << 2) ^ xs) | 0x20000u);
+  const uint32_t z = (a << 3) << m1;                 // exponent (3 bits), then the fraction
+  uint32_t fb;                                       // (z >> 6) + (138 << 23)
+#if defined(__CUDA_ARCH__)
+  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(fb) : "r"(z), "r"(1u << 26), "r"(138u << 23));
+  const float f = fmaf(__uint_as_float(fb), __uint_as_float(((uint32_t)c32 & 0x80000000u) | 0x3F800000u),
+                       12582912.0f);
+  v = __float_as_int(f) - 0x4B400000;
+#else
+  fb = (z >> 6) + (138u << 23);
+  float f;
+  memcpy(&f, &fb, 4);
+  f = (c32 < 0 ? -f : f) + 12582912.0f;
+  memcpy(&v, &f, 4);
+  v -= 0x4B400000;
+#endif
+  k = m1 ^ (int)~xs;                                 // ones: run - 1; zeros: -run
+}
+
 // from_quire<16>(quire_from_bp16(a) + quire_from_bp16(b), truncate) without
 // the 256-bit quire.  Each operand is m * 2^x (m < 2^13; zero and NaR count
 // as 0, and bits below 2^-96 are dropped as the per-value quire conversion

@@ -882,14 +882,15 @@ int mosyne_bposit16_table_host(int which, uint16_t* host_out) {
 int mosyne_bposit_debug_alu_check(int op, unsigned long long* host_out) {
   DeviceContext* ctx = ctx_get_or_init();
   if (!ctx) return RC_NOT_INIT;
-  if (op < 0 || op > 6 || !host_out) return RC_BAD_ARG;
+  if (op < 0 || op > 7 || !host_out) return RC_BAD_ARG;
   unsigned long long* d = nullptr;
   if (cudaMalloc(&d, 2 * sizeof(unsigned long long)) != cudaSuccess) return RC_ALLOC;
   const unsigned long long init[2] = {0ull, ~0ull};
   int rc = cudaMemcpy(d, init, sizeof(init), cudaMemcpyHostToDevice) == cudaSuccess ? RC_OK
                                                                                     : RC_LAUNCH;
   if (rc == RC_OK)
-    rc = op >= 4 ? div_check_run(ctx, d, 0, op - 4) : alu_check_run(ctx, op, d, 0);
+    rc = op == 7 ? sum_bin_check_run(d, 0)
+                 : op >= 4 ? div_check_run(ctx, d, 0, op - 4) : alu_check_run(ctx, op, d, 0);
   if (rc == RC_OK && cudaMemcpy(host_out, d, sizeof(init), cudaMemcpyDeviceToHost) != cudaSuccess)
     rc = RC_LAUNCH;
   cudaFree(d);

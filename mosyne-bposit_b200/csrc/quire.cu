@@ -5,7 +5,7 @@
 // correct for one warp) and the <=32-block entropy reduction
 // (kernels/shannon_entropy_bposit16.cu:45-119) with a grid-wide one:
 // 16-byte streaming loads of 8 codes, an arithmetic bposit16 decode (no
-// 2 MiB table) into per-regime int64 sums kept in shared memory, folded once
+// 2 MiB table) into per-regime int32 sums kept in shared memory, folded once
 // per thread into a 256-bit quire, then warp shuffles, a shared-memory block
 // step, per-block partials and a last-block finish.  Integer addition is
 // associative, so the quire (and every encoding of it) is identical for any
@@ -19,75 +19,54 @@ namespace {
 
 using bp::quire256;
 
-__device__ __forceinline__ void q_accumulate_bp16(quire256& acc, uint32_t code) {
-  const bp::Dec16 d = bp::decode16(code);
-  if (d.zero || d.nar) return;
-  int sh = d.exp2 + bp::kQuireFracBits;
-  uint64_t m = d.mant;
-  if (sh < 0) {
-    m = (-sh >= 32) ? 0ull : (m >> (-sh));
-    sh = 0;
-  }
-  const quire256 t = bp::q_from_shifted(m, sh);
-  acc = d.neg ? bp::q_sub(acc, t) : bp::q_add(acc, t);
-}
-
-// Per-regime integer sums.  For a bposit16 code with regime run length rs
-// (k = rs - 1 for a run of ones, -rs for zeros), shifting the 15-bit
-// magnitude left by 17 + rs + 1 leaves the exponent e in the top three bits
-// and the fraction left-aligned below it, so W = 1.f as an integer with 11
-// fraction bits (2^11 + f * 2^(11 - fw)) and
-//   value * 2^96 = (W << e) * 2^(8k + 85).
-// Within one regime the whole value is therefore V = W << e (< 2^19), and the
-// regime's sum is an ordinary integer sum of V.  Each thread keeps one int32
-// sum per regime k = -12 .. 14 in its own shared-memory column (exact for
+// Per-regime integer sums.  Within one regime k a bposit16 code's value is
+// the integer V = W << e (W = 1.f with 11 fraction bits, e the exponent) times
+// 2^(8k + 85 - 96) (bp::sum_bin16).  Each thread keeps one int32 sum per
+// regime k = -15 .. 14 in its own shared-memory column (exact for
 // 4096 values; folded into the 256-bit quire every 2048 values and at the
-// end), the decode is branch-free and the same for every code: zero, NaR and
-// regimes k < -12 (below 2^-96, adding nothing, as in the per-value
-// conversion, which truncates there) go to an extra bin that is never folded,
-// so every code takes one unconditional shared atomic.  For k = -12 and -11
-// every V is a multiple of the 2^11 / 2^3 the fold divides out, so the sum
-// stays exact.
-constexpr int kGroups = 28;          // bin 0: zero, NaR and regimes below -12 (dropped)
-constexpr int kGroupLow = -12;
+// end), the decode is branch-free and the same for every code: zero and NaR
+// (k = -15) and the regimes k = -14, -13 (below 2^-96, adding nothing, as in
+// the per-value conversion, which truncates there) have bins that are never
+// folded, so every code takes one unconditional shared atomic at its own k.
+// For k = -12 and -11 every V is a multiple of the 2^11 / 2^3 the fold
+// divides out, so the sum stays exact.
+constexpr int kGroups = 30;          // k = -15 .. 14
+constexpr int kGroupLow = -15;
+constexpr int kKeptLow = -12;        // bins below: zero, NaR, values under 2^-96
 constexpr int kFoldIters = 256;                          // x 8 codes per iteration
 
-// The group (regime bin) and signed within-regime value of one summand.
-__device__ __forceinline__ void group_decode(int code_sext, int& idx, int& v) {
-  const uint32_t rest = (uint32_t)abs(code_sext) & 0x7FFFu;   // zero and NaR: 0
-  const uint32_t y = rest << 17;
-  const int rs = __clz(y ^ (y << 1)) + 1;                 // regime run length
-  const uint32_t z = y << ((rs + 1) & 31);
-  const uint32_t e = z >> 29;
-  const int V = (int)(((((z >> 18) & 0x7FFu) | 0x800u)) << e);
-  const int k = (int)y < 0 ? rs - 1 : -rs;                // zero / NaR: rs = 33, k = -33
-  idx = max(k - kGroupLow + 1, 0);
-  const int sg = code_sext >> 31;
-  v = (V ^ sg) - sg;
+// c32: the summand's code in the upper 16 bits (bp::sum_bin16); gk: this
+// thread's sum for k = 0, the sum for k at gk[k * BS].
+template <int BS>   // the block size: stride between one thread's group sums
+__device__ __forceinline__ void group_accumulate_bp16(int* gk, int32_t c32) {
+  int k, v;
+  bp::sum_bin16(c32, k, v);
+  atomicAdd(gk + k * BS, v);
 }
 
-template <int BS>   // the block size: stride between one thread's group sums
-__device__ __forceinline__ void group_accumulate_bp16(int* g, int code_sext) {
-  int idx, v;
-  group_decode(code_sext, idx, v);
-  atomicAdd(g + idx * BS, v);
-}
+// -code in the upper 16 bits (the 32-bit negate of code << 16 is the
+// code's own negate; NaR stays NaR).
+__device__ __forceinline__ int32_t neg_hi(uint32_t code) { return (int32_t)(0u - (code << 16)); }
 
 // The entropy's summands pre-decoded: entry c (a probability code 0 .. 0x7FFF)
-// = the group and signed value of -term[c], packed as v << 5 | idx (0 for the
-// dropped bin); negative probability codes have the NaR term, which adds
+// = the regime and signed value of -term[c], packed as v << 5 | (k + 13)
+// (0: a summand that adds nothing); negative probability codes have the NaR term, which adds
 // nothing.  One shared load and one shared atomic per code in place of the
 // table load and the decode.
 __device__ __forceinline__ int term_dec_entry(uint32_t c, const uint16_t* term) {
-  int idx, v;
-  group_decode(-(int)(int16_t)term[c], idx, v);
-  return idx == 0 ? 0 : (int)((uint32_t)v << 5) | idx;
+  int k, v;
+  bp::sum_bin16(neg_hi(term[c]), k, v);
+  return k < kKeptLow ? 0 : (int)((uint32_t)v << 5) | (k - kKeptLow + 1);
 }
 
+__device__ __forceinline__ int dec_entry(uint32_t code, const int* dec) {
+  return (code & 0x8000u) ? 0 : dec[code & 0x7FFFu];
+}
+
+// g0: this thread's sum for k = kKeptLow - 1 (a dropped bin, entry 0)
 template <int BS>
-__device__ __forceinline__ void group_accumulate_dec(int* g, uint32_t code, const int* dec) {
-  const int e = (code & 0x8000u) ? 0 : dec[code & 0x7FFFu];
-  atomicAdd(g + (e & 31) * BS, e >> 5);
+__device__ __forceinline__ void group_add_dec(int* g0, int e) {
+  atomicAdd(g0 + (e & 31) * BS, e >> 5);
 }
 
 // Also counts the negative probability codes whose term is not NaR (none in
@@ -102,14 +81,13 @@ __global__ void term_dec_build_kernel(const uint16_t* __restrict__ term, int* __
 }
 
 template <int BS>
-__device__ __forceinline__ quire256 fold_groups(int* g, quire256 q) {
-#pragma unroll 1
-  g[0] = 0;                                               // the dropped bin
-  for (int i = 1; i < kGroups; ++i) {
-    const int s = g[i * BS];
+__device__ __forceinline__ quire256 fold_groups(int* gk, quire256 q) {
+  for (int k = kGroupLow; k < kKeptLow; ++k) gk[k * BS] = 0;   // the dropped bins
+  for (int k = kKeptLow; k < kGroupLow + kGroups; ++k) {
+    const int s = gk[k * BS];
     if (s == 0) continue;
-    g[i * BS] = 0;
-    const int sh = 8 * (i - 1 + kGroupLow) + 85;          // -11 .. 197
+    gk[k * BS] = 0;
+    const int sh = 8 * k + 85;                            // -11 .. 197
     uint64_t mag = s < 0 ? (uint64_t)(-(long long)s) : (uint64_t)s;
     int shp = sh;
     if (shp < 0) {
@@ -156,9 +134,9 @@ enum SumMode { SUM_PLAIN = 0, SUM_TERM_L2 = 1, SUM_TERM_SMEM = 2 };
 constexpr int kTermTableBytes = 65536 * 2;
 
 template <int MODE>
-__device__ __forceinline__ int summand(uint32_t code, const uint16_t* __restrict__ tab) {
-  if (MODE == SUM_TERM_L2) return -(int)(int16_t)__ldg(tab + code);
-  return -(int)(int16_t)tab[code];
+__device__ __forceinline__ int32_t summand(uint32_t code, const uint16_t* __restrict__ tab) {
+  if (MODE == SUM_TERM_L2) return neg_hi(__ldg(tab + code));
+  return neg_hi(tab[code]);
 }
 
 template <int MODE>
@@ -172,10 +150,11 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
     quire256* __restrict__ partials,
     unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
     uint32_t* bp32_out, int rtne16, int rtne32) {
-  __shared__ quire256 sh[32];
   __shared__ bool is_last;
   extern __shared__ __align__(16) uint8_t sum_smem_raw[];   // [kGroups][BS] int, then the table
   int* g = reinterpret_cast<int*>(sum_smem_raw) + threadIdx.x;
+  int* gk = g - kGroupLow * BS;                             // this thread's sum for k = 0
+  int* g0 = g + (kKeptLow - 1 - kGroupLow) * BS;            // k = kKeptLow - 1
   const uint16_t* tab = term;
   if (MODE == SUM_TERM_SMEM) {
     uint4* dst = reinterpret_cast<uint4*>(sum_smem_raw + (size_t)kGroups * BS * sizeof(int));
@@ -206,26 +185,42 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
       for (int u = 0; u < U; ++u)
         r[u] = (U == 1 || i0 + u * stride < nv) ? __ldcs(xv + i0 + u * stride)
                                                 : make_uint4(0u, 0u, 0u, 0u);
+      if (MODE == SUM_TERM_SMEM) {
+        // every lookup first, then the atomics: table and sums share the
+        // shared memory, so the compiler keeps program order between a
+        // lookup and an earlier atomic, and interleaved they would wait on
+        // one another
+        const int* dec = reinterpret_cast<const int*>(tab);
+        int e[U * 8];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+        for (int u = 0; u < U; ++u) {
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (MODE == SUM_TERM_SMEM) {
-            const int* dec = reinterpret_cast<const int*>(tab);
-            group_accumulate_dec<BS>(g, w[j] & 0xFFFFu, dec);
-            group_accumulate_dec<BS>(g, w[j] >> 16, dec);
-          } else if (MODE != SUM_PLAIN) {
-            group_accumulate_bp16<BS>(g, summand<MODE>(w[j] & 0xFFFFu, tab));
-            group_accumulate_bp16<BS>(g, summand<MODE>(w[j] >> 16, tab));
-          } else {
-            group_accumulate_bp16<BS>(g, (int)(w[j] << 16) >> 16);
-            group_accumulate_bp16<BS>(g, (int)w[j] >> 16);
+          for (int j = 0; j < 4; ++j) {
+            e[u * 8 + 2 * j] = dec_entry(w[j] & 0xFFFFu, dec);
+            e[u * 8 + 2 * j + 1] = dec_entry(w[j] >> 16, dec);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < U * 8; ++i) group_add_dec<BS>(g0, e[i]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (MODE != SUM_PLAIN) {
+              group_accumulate_bp16<BS>(gk, summand<MODE>(w[j] & 0xFFFFu, tab));
+              group_accumulate_bp16<BS>(gk, summand<MODE>(w[j] >> 16, tab));
+            } else {
+              group_accumulate_bp16<BS>(gk, (int32_t)(w[j] << 16));
+              group_accumulate_bp16<BS>(gk, (int32_t)(w[j] & 0xFFFF0000u));
+            }
           }
         }
       }
       if (++iters == kFoldIters / U) {     // every 2048 codes per thread
-        acc = fold_groups<BS>(g, acc);
+        acc = fold_groups<BS>(gk, acc);
         iters = 0;
       }
     }
@@ -233,12 +228,17 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
   }
   for (size_t i = done + tid; i < n; i += stride) {
     if (MODE == SUM_TERM_SMEM)
-      group_accumulate_dec<BS>(g, x[i], reinterpret_cast<const int*>(tab));
+      group_add_dec<BS>(g0, dec_entry(x[i], reinterpret_cast<const int*>(tab)));
     else
-      group_accumulate_bp16<BS>(g, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab) : (int)(int16_t)x[i]);
+      group_accumulate_bp16<BS>(gk, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab)
+                                                     : (int32_t)((uint32_t)x[i] << 16));
   }
-  acc = fold_groups<BS>(g, acc);
+  acc = fold_groups<BS>(gk, acc);
 
+  // the block step's 32 quires reuse the start of the (now dead) group sums,
+  // which keeps 7 blocks of 256 threads resident per SM
+  quire256* sh = reinterpret_cast<quire256*>(sum_smem_raw);
+  __syncthreads();
   acc = block_reduce_q(acc, sh);
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = acc;
@@ -262,6 +262,35 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
     if (bp16_out) *bp16_out = (uint16_t)bp::from_quire<16>(q, rtne16);
     if (bp32_out) *bp32_out = bp::from_quire<32>(q, rtne32);
     *ticket = 0u;  // ready for the next call
+  }
+}
+
+// Every bposit16 code through the exact sum's device decode (bp::sum_bin16)
+// against its quire image (bp::quire_from_bp16), as a regime sum folds it:
+// res[0] = mismatches, res[1] = the lowest failing code.
+__global__ void sum_bin_check_kernel(unsigned long long* res) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 65536u) return;
+  int k, v;
+  bp::sum_bin16((int32_t)(c << 16), k, v);
+  quire256 r = bp::q_zero();
+  bool ok = k >= kGroupLow && k < kGroupLow + kGroups && ((c & 0x7FFFu) != 0u || k < kKeptLow);
+  if (k >= kKeptLow) {
+    int sh = 8 * k + 85;
+    uint64_t m = (uint64_t)(v < 0 ? -(long long)v : (long long)v);
+    if (sh < 0) {
+      ok = ok && (m & ((1ull << -sh) - 1)) == 0;
+      m >>= -sh;
+      sh = 0;
+    }
+    r = bp::q_from_shifted(m, sh);
+    if (v < 0) r = bp::q_neg(r);
+  }
+  const quire256 q = bp::quire_from_bp16(c);
+  for (int i = 0; i < 4; ++i) ok = ok && q.w[i] == r.w[i];
+  if (!ok) {
+    atomicAdd(res, 1ull);
+    atomicMin(res + 1, (unsigned long long)c);
   }
 }
 
@@ -522,6 +551,11 @@ int term_dec_build(const uint16_t* term, int* out, bool* usable) {
   cudaFree(bad);
   *usable = rc == RC_OK && h == 0;
   return rc;
+}
+
+int sum_bin_check_run(unsigned long long* res, cudaStream_t st) {
+  sum_bin_check_kernel<<<256, 256, 0, st>>>(res);
+  return launch_rc();
 }
 
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,

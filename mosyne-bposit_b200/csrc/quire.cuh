@@ -16,6 +16,9 @@ int shannon_entropy_bp16_run(DeviceContext* ctx, const uint16_t* p, size_t n,
 // (device init; term = the entropy term table); `usable` false when a
 // negative code's term is not NaR (the staged mode then is not used).
 int term_dec_build(const uint16_t* term, int* out, bool* usable);
+// The exact sum's per-code decode on the device against the quire image of
+// every bposit16 code: res[0] = mismatches, res[1] = the lowest failing code.
+int sum_bin_check_run(unsigned long long* res, cudaStream_t st);
 int fp32_atomic_sum_run(DeviceContext* ctx, const float* x, size_t n, float* acc,
                         cudaStream_t st);
 int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void* out, int nbits,

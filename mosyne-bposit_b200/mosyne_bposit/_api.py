@@ -455,11 +455,13 @@ def debug_alu_check(op: str) -> tuple:
     forms over all 2^32 code pairs ("add", "mul_exact", "quire_sum" or "mul"),
     or the GEMM epilogues' divisions against the IEEE division on 2^32
     pseudo-random operand pairs ("dequant_div", "silu_div"), and that divide's
-    reciprocal step on every normal divisor in its range ("div_reciprocal"):
-    returns (mismatching pairs, first mismatching pair index or None)."""
+    reciprocal step on every normal divisor in its range ("div_reciprocal"),
+    or the exact sum's per-code decode against the quire image of every
+    bposit16 code ("sum_decode"): returns (mismatches, first mismatching
+    pair, operand or code, or None)."""
     out = np.zeros(2, dtype=np.uint64)
     idx = ("add", "mul_exact", "quire_sum", "mul", "dequant_div", "silu_div",
-           "div_reciprocal").index(op)
+           "div_reciprocal", "sum_decode").index(op)
     _check(_ensure_library().mosyne_bposit_debug_alu_check(idx, out.ctypes.data),
            "mosyne_bposit_debug_alu_check")
     first = int(out[1])

@@ -196,6 +196,35 @@ size_t h_from_float_tab_exhaustive() {
   return bad;
 }
 
+// Mismatches of the exact sum's regime-bin decode against quire_from_bp16 over
+// every code: regime k >= -12 and value v stand for v * 2^(8k + 85) in the
+// quire's units; k = -15 (zero, NaR) and -14, -13 for summands the quire
+// conversion maps to zero; no other k.
+size_t h_sum_bin16_check() {
+  size_t bad = 0;
+  for (uint32_t c = 0; c < 65536; ++c) {
+    int k, v;
+    bp::sum_bin16((int32_t)(c << 16), k, v);
+    if (k < -15 || k > 14) ++bad;
+    if ((c & 0x7FFFu) == 0 && k != -15) ++bad;
+    bp::quire256 r = bp::q_zero();
+    if (k >= -12) {
+      int sh = 8 * k + 85;
+      uint64_t m = (uint64_t)(v < 0 ? -(int64_t)v : (int64_t)v);
+      if (sh < 0) {
+        if (m & ((1ull << -sh) - 1)) ++bad;   // the fold's right shift must be exact
+        m >>= -sh;
+        sh = 0;
+      }
+      r = bp::q_from_shifted(m, sh);
+      if (v < 0) r = bp::q_neg(r);
+    }
+    const bp::quire256 q = bp::quire_from_bp16(c);
+    if (memcmp(&q, &r, sizeof q) != 0) ++bad;
+  }
+  return bad;
+}
+
 void h_quire_sum(const uint16_t* p, size_t n, uint64_t* w) {
   bp::quire256 acc = bp::q_zero();
   for (size_t i = 0; i < n; ++i) acc = bp::q_add(acc, bp::quire_from_bp16(p[i]));

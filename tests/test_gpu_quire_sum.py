@@ -103,6 +103,21 @@ def test_exact_sum_every_code(cuda_lib):
     assert b16 == 0x7FFF
 
 
+def test_exact_sum_decode_every_code(cuda_lib):
+    """The device decode each code takes in the exact sum (its regime and the
+    signed integer within the regime, formed through one fused multiply-add)
+    equals the code's quire image for all 65,536 codes; a sum over every code
+    cannot show this, as each code cancels against its negation."""
+    from mosyne_bposit import _api
+    bad, first = _api.debug_alu_check("sum_decode")
+    assert bad == 0, (bad, first)
+    pos = np.arange(1, 0x8000, dtype=np.uint16)
+    q, _, _ = _sum(pos)
+    assert q == sum(O.bposit16_to_quire(p) for p in range(1, 0x8000))
+    q, _, _ = _sum((0x10000 - pos.astype(np.uint32)).astype(np.uint16)[::3])
+    assert q == -sum(O.bposit16_to_quire(p) for p in range(1, 0x8000, 3))
+
+
 def test_exact_sum_large_inputs(cuda_lib):
     """Millions of codes: every code (zero, NaR, both extremes of the regime
     range) many times over, a sign-cancelling mix, an unaligned start with an

@@ -211,6 +211,14 @@ def test_float_table_encoder_every_pattern(hlib):
     assert hlib.h_from_float_tab_exhaustive() == 0
 
 
+def test_sum_regime_bins_every_code(hlib):
+    """The exact sum's branch-free decode (regime bin and signed within-regime
+    integer, folded as v * 2^(8k + 85) into the quire) equals quire_from_bp16 on
+    every code, and the fold's right shift for the lowest regimes drops no bit."""
+    hlib.h_sum_bin16_check.restype = ctypes.c_size_t
+    assert hlib.h_sum_bin16_check() == 0
+
+
 def test_quire_halves_every_code(hlib):
     """The element-wise bposit16 -> quire kernel's per-lane half (32-bit words,
     two's complement carried across the halves) equals quire_from_bp16 on
