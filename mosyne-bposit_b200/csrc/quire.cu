@@ -122,6 +122,55 @@ __device__ __forceinline__ quire256 block_reduce_q(quire256 q, quire256* sh /*[3
   return q;  // valid in thread 0
 }
 
+// The block's sum, valid in thread 0: each kept regime's sums over all the
+// block's threads added in int64 by one warp (exact: a thread's sum is below
+// 2^19 * 4096, the block's below 2^40) and placed into that warp's quire
+// once, plus the quires of threads that folded during the loop.  In place of
+// every thread folding its own 27 sums into a quire -- as many instructions
+// as summing ~60 codes, when an input of 2^24 codes gives each thread ~70.
+// g: the block's group sums ([kGroups][BS] int); sh: 32 quires of scratch,
+// which may alias g.
+template <int BS>
+__device__ __forceinline__ quire256 block_fold_q(const int* g, quire256 acc, quire256* sh) {
+  constexpr int NW = BS / 32;
+  const bool any_acc = __syncthreads_or(!bp::q_is_zero(acc));   // also: every sum final
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  quire256 qb = bp::q_zero();
+  for (int k = kKeptLow + warp; k < kGroupLow + kGroups; k += NW) {
+    const int* col = g + (k - kGroupLow) * BS;
+    long long s = 0;
+#pragma unroll
+    for (int j = 0; j < BS / 32; ++j) s += col[lane + 32 * j];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (s != 0) {
+      uint64_t mag = s < 0 ? (uint64_t)(-s) : (uint64_t)s;
+      int sh8 = 8 * k + 85;                               // -11 .. 197
+      if (sh8 < 0) {
+        mag >>= -sh8;                                     // exact: every V is a multiple
+        sh8 = 0;
+      }
+      const quire256 t = bp::q_from_shifted(mag, sh8);
+      qb = s < 0 ? bp::q_sub(qb, t) : bp::q_add(qb, t);
+    }
+  }
+  quire256 q = lane == 0 ? qb : bp::q_zero();
+  if (any_acc) {
+    q = bp::q_add(q, acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q = bp::q_add(q, shfl_down_q(q, off));
+  }
+  __syncthreads();                                        // every sum read before sh is written
+  if (lane == 0) sh[warp] = q;
+  __syncthreads();
+  if (warp == 0) {
+    q = lane < NW ? sh[lane] : bp::q_zero();
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q = bp::q_add(q, shfl_down_q(q, off));
+  }
+  return q;
+}
+
 // Summand modes.  SUM_PLAIN: the codes themselves.  SUM_TERM_L2 /
 // SUM_TERM_SMEM: each code p is replaced by -term[p] before it is summed, so
 // the quire holds H = -sum p log2(p) (kernels/shannon_entropy_bposit16.cu:
@@ -144,8 +193,11 @@ constexpr size_t sum_smem(int bs) {
   return (size_t)kGroups * bs * sizeof(int) + (MODE == SUM_TERM_SMEM ? kTermTableBytes : 0);
 }
 
+// Registers: 6 blocks of 256 per SM for the decoding modes (40 a thread with
+// the loads of the next iteration in flight); the staged-table mode runs one
+// 512-thread block per SM and may use 78 (its 32 lookups held before the atomics).
 template <int MODE, int BS>
-__global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
+__global__ void __launch_bounds__(BS, MODE == SUM_TERM_SMEM ? 1 : 6) quire_sum_bp16_kernel(
     const uint16_t* __restrict__ x, size_t n, const uint16_t* __restrict__ term,
     quire256* __restrict__ partials,
     unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
@@ -179,12 +231,20 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
     // nothing in every mode (zero, or the NaR term of zero)
     constexpr int U = MODE == SUM_TERM_SMEM ? 4 : 1;
     int iters = 0;
+    // the next iteration's loads are issued before this one's codes are
+    // summed, so the HBM latency overlaps the integer work
+    uint4 nx[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      nx[u] = tid + u * stride < nv ? __ldcs(xv + tid + u * stride) : make_uint4(0u, 0u, 0u, 0u);
     for (size_t i0 = tid; i0 < nv; i0 += U * stride) {
       uint4 r[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        r[u] = (U == 1 || i0 + u * stride < nv) ? __ldcs(xv + i0 + u * stride)
-                                                : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < U; ++u) {
+        r[u] = nx[u];
+        const size_t in = i0 + (U + u) * stride;
+        nx[u] = in < nv ? __ldcs(xv + in) : make_uint4(0u, 0u, 0u, 0u);
+      }
       if (MODE == SUM_TERM_SMEM) {
         // every lookup first, then the atomics: table and sums share the
         // shared memory, so the compiler keeps program order between a
@@ -233,13 +293,9 @@ __global__ void __launch_bounds__(BS) quire_sum_bp16_kernel(
       group_accumulate_bp16<BS>(gk, MODE != SUM_PLAIN ? summand<MODE>(x[i], tab)
                                                      : (int32_t)((uint32_t)x[i] << 16));
   }
-  acc = fold_groups<BS>(gk, acc);
-
-  // the block step's 32 quires reuse the start of the (now dead) group sums,
-  // which keeps 7 blocks of 256 threads resident per SM
+  // the block step's 32 quires reuse the start of the (now dead) group sums
   quire256* sh = reinterpret_cast<quire256*>(sum_smem_raw);
-  __syncthreads();
-  acc = block_reduce_q(acc, sh);
+  acc = block_fold_q<BS>(g - threadIdx.x, acc, sh);
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = acc;
     __threadfence();
