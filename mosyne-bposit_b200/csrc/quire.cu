@@ -171,6 +171,39 @@ __device__ __forceinline__ quire256 block_fold_q(const int* g, quire256 acc, qui
   return q;
 }
 
+// The grid step: thread 0 of each block publishes the block's quire (acc,
+// valid in thread 0), and the last block to arrive (ticket) adds all of them
+// in a fixed order and writes the quire and its encodings.
+__device__ __forceinline__ void grid_finish(const quire256& acc, quire256* sh, bool* is_last,
+                                            quire256* __restrict__ partials,
+                                            unsigned int* __restrict__ ticket,
+                                            quire256* __restrict__ q_out, uint16_t* bp16_out,
+                                            uint32_t* bp32_out, int rtne16, int rtne32) {
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = acc;
+    __threadfence();
+    const unsigned int t = atomicAdd(ticket, 1u);
+    *is_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!*is_last) return;
+  __threadfence();
+  quire256 q = bp::q_zero();
+  for (unsigned int i = threadIdx.x; i < gridDim.x; i += blockDim.x) {
+    const volatile uint64_t* pw = reinterpret_cast<volatile uint64_t*>(&partials[i]);
+    const quire256 v = {{pw[0], pw[1], pw[2], pw[3]}};
+    q = bp::q_add(q, v);
+  }
+  __syncthreads();
+  q = block_reduce_q(q, sh);
+  if (threadIdx.x == 0) {
+    if (q_out) *q_out = q;
+    if (bp16_out) *bp16_out = (uint16_t)bp::from_quire<16>(q, rtne16);
+    if (bp32_out) *bp32_out = bp::from_quire<32>(q, rtne32);
+    *ticket = 0u;  // ready for the next call
+  }
+}
+
 // Summand modes.  SUM_PLAIN: the codes themselves.  SUM_TERM_L2 /
 // SUM_TERM_SMEM: each code p is replaced by -term[p] before it is summed, so
 // the quire holds H = -sum p log2(p) (kernels/shannon_entropy_bposit16.cu:
@@ -193,9 +226,10 @@ constexpr size_t sum_smem(int bs) {
   return (size_t)kGroups * bs * sizeof(int) + (MODE == SUM_TERM_SMEM ? kTermTableBytes : 0);
 }
 
-// Registers: 6 blocks of 256 per SM for the decoding modes (40 a thread with
-// the loads of the next iteration in flight); the staged-table mode runs one
-// 512-thread block per SM and may use 78 (its 32 lookups held before the atomics).
+// Registers: at most 40 a thread for the decoding modes (6 blocks of 256
+// could be resident; the launch uses 3 per SM); the staged-table mode runs
+// one 512-thread block per SM and may use 78 (its 32 lookups held before the
+// atomics).
 template <int MODE, int BS>
 __global__ void __launch_bounds__(BS, MODE == SUM_TERM_SMEM ? 1 : 6) quire_sum_bp16_kernel(
     const uint16_t* __restrict__ x, size_t n, const uint16_t* __restrict__ term,
@@ -296,29 +330,7 @@ __global__ void __launch_bounds__(BS, MODE == SUM_TERM_SMEM ? 1 : 6) quire_sum_b
   // the block step's 32 quires reuse the start of the (now dead) group sums
   quire256* sh = reinterpret_cast<quire256*>(sum_smem_raw);
   acc = block_fold_q<BS>(g - threadIdx.x, acc, sh);
-  if (threadIdx.x == 0) {
-    partials[blockIdx.x] = acc;
-    __threadfence();
-    const unsigned int t = atomicAdd(ticket, 1u);
-    is_last = (t == gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  quire256 q = bp::q_zero();
-  for (unsigned int i = threadIdx.x; i < gridDim.x; i += blockDim.x) {
-    const volatile uint64_t* pw = reinterpret_cast<volatile uint64_t*>(&partials[i]);
-    const quire256 v = {{pw[0], pw[1], pw[2], pw[3]}};
-    q = bp::q_add(q, v);
-  }
-  __syncthreads();
-  q = block_reduce_q(q, sh);
-  if (threadIdx.x == 0) {
-    if (q_out) *q_out = q;
-    if (bp16_out) *bp16_out = (uint16_t)bp::from_quire<16>(q, rtne16);
-    if (bp32_out) *bp32_out = bp::from_quire<32>(q, rtne32);
-    *ticket = 0u;  // ready for the next call
-  }
+  grid_finish(acc, sh, &is_last, partials, ticket, q_out, bp16_out, bp32_out, rtne16, rtne32);
 }
 
 // Every bposit16 code through the exact sum's device decode (bp::sum_bin16)
@@ -548,7 +560,7 @@ int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint
                      mosyne_quire256* q_out, uint16_t* bp16_out, uint32_t* bp32_out, int flags,
                      cudaStream_t st, int max_blocks) {
   if (n > 0 && !x) return RC_BAD_ARG;
-  // group sums 27 KiB per 256 threads (+ the 128 KiB term table when staged)
+  // group sums 30 KiB per 256 threads (+ the 128 KiB term table when staged)
   constexpr int kSumSmem = (int)sum_smem<MODE>(BS);
   static_assert(kSumSmem <= 227 * 1024, "shared memory");
   if (ensure_smem_attr((const void*)quire_sum_bp16_kernel<MODE, BS>, kSumSmem) != RC_OK)
@@ -557,6 +569,11 @@ int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint
   // every block resident at once (shared memory bounds the blocks per SM)
   size_t cap = (size_t)resident_blocks((const void*)quire_sum_bp16_kernel<MODE, BS>, BS, kSumSmem,
                                        ctx->num_sms);
+  // decoding modes: 3 blocks (24 warps) per SM, with the next load in flight,
+  // cover the HBM latency; more threads only add their per-thread set-up
+  // and fold (2^24 codes: 26.7 us with 6 blocks per SM, 24.8 with 3, 27.9
+  // with 2, measured on B200)
+  if (MODE != SUM_TERM_SMEM && cap > (size_t)ctx->num_sms * 3) cap = (size_t)ctx->num_sms * 3;
   if (max_blocks > 0 && (size_t)max_blocks < cap) cap = (size_t)max_blocks;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
