@@ -236,6 +236,12 @@ __global__ void __launch_bounds__(BS, MODE == SUM_TERM_SMEM ? 1 : 6) quire_sum_b
     quire256* __restrict__ partials,
     unsigned int* __restrict__ ticket, quire256* __restrict__ q_out, uint16_t* bp16_out,
     uint32_t* bp32_out, int rtne16, int rtne32) {
+  // launched as a programmatic dependent: the set-up below (the group sums
+  // cleared, the staged table copied: constant since the device was set up)
+  // overlaps the previous kernel's tail; griddepcontrol.wait then waits for
+  // that kernel to complete before the codes, the partials or the ticket are
+  // touched.  The next kernel may start its own set-up at once.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ bool is_last;
   extern __shared__ __align__(16) uint8_t sum_smem_raw[];   // [kGroups][BS] int, then the table
   int* g = reinterpret_cast<int*>(sum_smem_raw) + threadIdx.x;
@@ -251,6 +257,7 @@ __global__ void __launch_bounds__(BS, MODE == SUM_TERM_SMEM ? 1 : 6) quire_sum_b
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) g[i * BS] = 0;
   if (MODE == SUM_TERM_SMEM) __syncthreads();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   quire256 acc = bp::q_zero();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -579,11 +586,26 @@ int quire_sum_launch(DeviceContext* ctx, const uint16_t* x, size_t n, const uint
   if (blocks == 0) blocks = 1;
   if (ensure_scratch(&ctx->partials, &ctx->partials_bytes, blocks * sizeof(quire256)))
     return RC_ALLOC;
-  quire_sum_bp16_kernel<MODE, BS><<<(unsigned)blocks, BS, kSumSmem, st>>>(
-      x, n, term, static_cast<quire256*>(ctx->partials), ctx->ticket,
-      reinterpret_cast<quire256*>(q_out), bp16_out, bp32_out, (flags & MOSYNE_RTNE_BP16) != 0,
-      (flags & MOSYNE_RTNE_BP32) != 0);
-  return launch_rc();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(BS, 1, 1);
+  cfg.dynamicSmemBytes = kSumSmem;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const uint16_t* xc = x;
+  quire256* part = static_cast<quire256*>(ctx->partials);
+  quire256* qo = reinterpret_cast<quire256*>(q_out);
+  const int r16 = (flags & MOSYNE_RTNE_BP16) != 0, r32 = (flags & MOSYNE_RTNE_BP32) != 0;
+  if (cudaLaunchKernelEx(&cfg, quire_sum_bp16_kernel<MODE, BS>, xc, n, term, part, ctx->ticket, qo,
+                         bp16_out, bp32_out, r16, r32) != cudaSuccess) {
+    cudaGetLastError();            // a refused launch must not fail the next one
+    return RC_LAUNCH;
+  }
+  return RC_OK;
 }
 
 }  // namespace
