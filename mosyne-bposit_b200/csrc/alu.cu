@@ -144,6 +144,11 @@ __global__ void __launch_bounds__(1024) ew_kernel(const uint16_t* __restrict__ a
                                                   uint16_t* __restrict__ out,
                                                   const uint16_t* __restrict__ t0,
                                                   const uint16_t* __restrict__ t1) {
+  // launched as a programmatic dependent: the tables (built when the device
+  // was set up, constant since) are staged while the previous kernel drains;
+  // griddepcontrol.wait precedes every read of the operands and every write
+  // of the output.  The next kernel may start its own staging at once.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int U = ew_unroll<OP>();
   extern __shared__ __align__(16) uint16_t s_tab[];
   // the truncated-sum encoder's table (add and the log/exp multiplier)
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(1024) ew_kernel(const uint16_t* __restrict__ a
     __syncthreads();
     tab = s_tab;
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   const bool vec = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(out) |
@@ -202,16 +208,33 @@ int launch_ew(DeviceContext* ctx, const uint16_t* a, const uint16_t* b, size_t n
   if (!a || !out) return RC_BAD_ARG;
   const bool table_op = (OP == OP_LUT || OP == OP_MUL || OP == OP_ADD);
   const bool stage = table_op && n >= (size_t)ctx->num_sms * 16384;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (stage) {
     // one CTA of 1024 threads per SM holding the 128 KiB table
     if (ensure_smem_attr((const void*)ew_kernel<OP, true>, TAB_BYTES) != RC_OK) return RC_LAUNCH;
-    ew_kernel<OP, true><<<ctx->num_sms, 1024, TAB_BYTES, st>>>(a, b, n, out, t0, t1);
+    cfg.gridDim = dim3((unsigned)ctx->num_sms, 1, 1);
+    cfg.blockDim = dim3(1024, 1, 1);
+    cfg.dynamicSmemBytes = TAB_BYTES;
+    e = cudaLaunchKernelEx(&cfg, ew_kernel<OP, true>, a, b, n, out, t0, t1);
   } else {
-    const unsigned blocks = stream_grid((const void*)ew_kernel<OP, false>, 256, 0, ctx->num_sms,
-                                        (n + 8 * 256 - 1) / (8 * 256));
-    ew_kernel<OP, false><<<blocks, 256, 0, st>>>(a, b, n, out, t0, t1);
+    cfg.gridDim = dim3(stream_grid((const void*)ew_kernel<OP, false>, 256, 0, ctx->num_sms,
+                                   (n + 8 * 256 - 1) / (8 * 256)), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    e = cudaLaunchKernelEx(&cfg, ew_kernel<OP, false>, a, b, n, out, t0, t1);
   }
-  return launch_rc();
+  if (e != cudaSuccess) {
+    cudaGetLastError();            // a refused launch must not fail the next one
+    return RC_LAUNCH;
+  }
+  return RC_OK;
 }
 
 __global__ void dec16_build_kernel(uint32_t* out, uint32_t* log_out, const uint16_t* lg) {
