@@ -118,6 +118,32 @@ inline cudaStream_t as_stream(mosyne_stream_t s) { return reinterpret_cast<cudaS
 
 inline int launch_rc() { return cudaGetLastError() == cudaSuccess ? RC_OK : RC_LAUNCH; }
 
+// Programmatic dependent launch of a stream kernel: it may start (and run its
+// set-up) while the previous kernel in the stream drains.  The kernel calls
+// pdl_release() first (so the next kernel may start the same way) and
+// pdl_wait() before its first global-memory access, which waits for the
+// previous kernel to complete and its writes to be visible.  A refused launch
+// is reported by launch_rc().
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_dependent(void (*kern)(KArgs...), unsigned grid, unsigned block,
+                             cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
 template <>

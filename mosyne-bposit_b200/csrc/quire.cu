@@ -388,6 +388,8 @@ constexpr int kEwUnroll = 4;
 template <int NB, bool RTNE, bool VEC>
 __global__ void __launch_bounds__(256) quire_to_bp_kernel(const quire256* __restrict__ q, size_t n,
                                                           void* out) {
+  pdl_release();
+  pdl_wait();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i0 = tid; i0 < n; i0 += kEwUnroll * stride) {
@@ -424,6 +426,8 @@ __global__ void __launch_bounds__(256) quire_to_bp_kernel(const quire256* __rest
 template <bool VEC>
 __global__ void __launch_bounds__(256) bp16_to_quire_kernel(const uint16_t* __restrict__ x,
                                                             size_t n, quire256* __restrict__ out) {
+  pdl_release();
+  pdl_wait();
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t tid = t >> 1;                                // code index of this lane pair
   const int half = (int)(t & 1);
@@ -466,9 +470,11 @@ template <bool RTNE>
 __global__ void __launch_bounds__(256) int32_to_bp32_tab_kernel(const int32_t* __restrict__ in,
                                                                 size_t n, size_t nv, int shift,
                                                                 uint32_t* __restrict__ out) {
+  pdl_release();
   __shared__ bp::I32Entry tab[33];
   if (threadIdx.x < 33) tab[threadIdx.x] = bp::i32_table_entry<32>(threadIdx.x, shift);
   __syncthreads();
+  pdl_wait();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   const int4* iv = reinterpret_cast<const int4*>(in);
@@ -510,9 +516,11 @@ __device__ __forceinline__ void store4_bp(void* out, size_t i, float4 f, const b
 template <int NB, bool RTNE>
 __global__ void __launch_bounds__(256) float_to_bp_f32_kernel(const float* __restrict__ x, size_t n,
                                                               size_t nv, void* out) {
+  pdl_release();
   __shared__ bp::F32Entry tab[256];
   tab[threadIdx.x] = bp::f32_table_entry<NB>((int)threadIdx.x);   // 256 threads
   __syncthreads();
+  pdl_wait();
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   const float4* xv = reinterpret_cast<const float4*>(x);
@@ -666,10 +674,10 @@ int quire_to_bp_run(DeviceContext* ctx, const mosyne_quire256* q, size_t n, void
   auto sg = [&](const void* k) { return stream_grid(k, 256, 0, ctx->num_sms, (n + 255) / 256); };
   const bool v = aligned16(q);
 #define MB_Q2B(NB, R)                                                                          \
-  (v ? quire_to_bp_kernel<NB, R, true><<<sg((const void*)quire_to_bp_kernel<NB, R, true>), 256, 0, \
-                                          st>>>(qq, n, out)                                    \
-     : quire_to_bp_kernel<NB, R, false><<<sg((const void*)quire_to_bp_kernel<NB, R, false>), 256, \
-                                           0, st>>>(qq, n, out))
+  (v ? launch_dependent(quire_to_bp_kernel<NB, R, true>,                                       \
+                        sg((const void*)quire_to_bp_kernel<NB, R, true>), 256, st, qq, n, out) \
+     : launch_dependent(quire_to_bp_kernel<NB, R, false>,                                      \
+                        sg((const void*)quire_to_bp_kernel<NB, R, false>), 256, st, qq, n, out))
   if (nbits == 16) {
     if (rtne) MB_Q2B(16, true); else MB_Q2B(16, false);
   } else {
@@ -685,11 +693,13 @@ int bp16_to_quire_run(DeviceContext* ctx, const uint16_t* x, size_t n, mosyne_qu
   auto* o = reinterpret_cast<quire256*>(out);
   const size_t work = (2 * n + 255) / 256;                 // two lanes per code
   if (aligned16(out))
-    bp16_to_quire_kernel<true><<<stream_grid((const void*)bp16_to_quire_kernel<true>, 256, 0,
-                                             ctx->num_sms, work), 256, 0, st>>>(x, n, o);
+    launch_dependent(bp16_to_quire_kernel<true>,
+                     stream_grid((const void*)bp16_to_quire_kernel<true>, 256, 0, ctx->num_sms, work),
+                     256, st, x, n, o);
   else
-    bp16_to_quire_kernel<false><<<stream_grid((const void*)bp16_to_quire_kernel<false>, 256, 0,
-                                              ctx->num_sms, work), 256, 0, st>>>(x, n, o);
+    launch_dependent(bp16_to_quire_kernel<false>,
+                     stream_grid((const void*)bp16_to_quire_kernel<false>, 256, 0, ctx->num_sms, work),
+                     256, st, x, n, o);
   return launch_rc();
 }
 
@@ -703,11 +713,13 @@ int int32_to_bp32_run(DeviceContext* ctx, const int32_t* in, size_t n, int shift
   const size_t nv = (aligned16(in) && aligned16(out)) ? n / 4 : 0;
   const size_t work = ((nv ? nv : n) + 255) / 256;
   if (rtne)
-    int32_to_bp32_tab_kernel<true><<<stream_grid((const void*)int32_to_bp32_tab_kernel<true>, 256, 0,
-                                                 ctx->num_sms, work), 256, 0, st>>>(in, n, nv, shift, out);
+    launch_dependent(int32_to_bp32_tab_kernel<true>,
+                     stream_grid((const void*)int32_to_bp32_tab_kernel<true>, 256, 0, ctx->num_sms, work),
+                     256, st, in, n, nv, shift, out);
   else
-    int32_to_bp32_tab_kernel<false><<<stream_grid((const void*)int32_to_bp32_tab_kernel<false>, 256,
-                                                  0, ctx->num_sms, work), 256, 0, st>>>(in, n, nv, shift, out);
+    launch_dependent(int32_to_bp32_tab_kernel<false>,
+                     stream_grid((const void*)int32_to_bp32_tab_kernel<false>, 256, 0, ctx->num_sms, work),
+                     256, st, in, n, nv, shift, out);
   return launch_rc();
 }
 
@@ -721,8 +733,9 @@ int float_to_bposit_run(DeviceContext* ctx, const void* x, int dtype, size_t n, 
     const size_t nv = v ? n / 4 : 0;
     const size_t work = ((nv ? nv : n) + 255) / 256;
 #define MB_F2B(NB, R)                                                                          \
-  float_to_bp_f32_kernel<NB, R><<<stream_grid((const void*)float_to_bp_f32_kernel<NB, R>, 256, 0, \
-                                              ctx->num_sms, work), 256, 0, st>>>(xf, n, nv, out)
+  launch_dependent(float_to_bp_f32_kernel<NB, R>,                                              \
+                   stream_grid((const void*)float_to_bp_f32_kernel<NB, R>, 256, 0, ctx->num_sms, work), \
+                   256, st, xf, n, nv, out)
     if (nbits == 16) {
       if (rtne) MB_F2B(16, true); else MB_F2B(16, false);
     } else {
