@@ -56,12 +56,15 @@ __device__ __forceinline__ void bp8_seg_ends(const Bp8Table& tab, const Bp8Seg& 
 __global__ void __launch_bounds__(kBp8Threads) bp8_to_i8_kernel(
     const __grid_constant__ Bp8Table tab, Bp8Seg s0, Bp8Seg s1) {
   // a GEMM launched after this kernel as a programmatic dependent waits for
-  // it before reading anything; it may set itself up meanwhile
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // it before reading anything; it may set itself up meanwhile.  This kernel
+  // is launched the same way: its table is spread while the previous kernel
+  // drains, and it waits for that kernel before touching global memory.
+  pdl_release();
   extern __shared__ uint32_t lut[];
   for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x)
     lut[i] = (uint32_t)(uint8_t)tab.v[i >> 5];
   __syncthreads();
+  pdl_wait();
   const uint32_t lane4 = (threadIdx.x & 31u) * 4u;
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -131,7 +134,8 @@ int bp8_to_i8_pair_run(const uint8_t* in0, size_t n0, int8_t* out0, const uint8_
   const size_t work = nv ? nv : n0 + n1;
   const unsigned blocks = stream_grid((const void*)bp8_to_i8_kernel, kBp8Threads, kBp8SmemBytes,
                                       num_sms, (work + kBp8Threads - 1) / kBp8Threads);
-  bp8_to_i8_kernel<<<blocks, kBp8Threads, kBp8SmemBytes, st>>>(g_bp8_table, s0, s1);
+  launch_dependent_smem(bp8_to_i8_kernel, blocks, kBp8Threads, kBp8SmemBytes, st, g_bp8_table, s0,
+                        s1);
   return launch_rc();
 }
 

@@ -130,6 +130,22 @@ __device__ __forceinline__ void pdl_release() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
+inline void launch_dependent_smem(void (*kern)(KArgs...), unsigned grid, unsigned block,
+                                  size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <typename... KArgs, typename... Args>
 inline void launch_dependent(void (*kern)(KArgs...), unsigned grid, unsigned block,
                              cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
