@@ -16,8 +16,9 @@
 // prefetches its weights into L2, which is coherent, so no stale data can
 // result.  Each quantiser's own griddepcontrol.wait, before its first global
 // access, waits for the kernel before it to complete, so the GEMM's wait
-// covers every earlier kernel.  The quantiser of one row per block is itself
-// launched as a programmatic dependent, so its launch overlaps the previous
+// covers every earlier kernel.  The row quantisers (registers, a warp or a
+// block per row) are themselves launched as programmatic dependents, so
+// their launch overlaps the previous
 // kernel's tail (e.g. the previous layer's GEMM, which reads the int8
 // activations this kernel is about to write).
 // The one-row-per-block quantiser is launched so (8192 x 4096 fp32 per token
@@ -59,6 +60,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
                                                          const uint32_t* __restrict__ given_amax,
                                                          int amax_stride, int reverse) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
+  pdl_wait();
   constexpr int V = Vec<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = (reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x) * 8 + warp;
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(256) quant_row_block_kernel(
     const uint32_t* __restrict__ given_amax, int amax_stride, float* __restrict__ scalar_scale,
     int reverse) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
+  pdl_wait();
   constexpr int V = Vec<T>::N;
   __shared__ float red[8];
   const int row = reverse ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
@@ -696,22 +699,24 @@ int quant_rows_t(const void* x, int R, int C, int8_t* q, float* scale, const uin
   }
   if (R <= kBlockPerRowMax || scalar_scale) {
     if (vec)
-      quant_row_block_kernel<T, true><<<(unsigned)R, 256, 0, st>>>(
-          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale, reverse);
+      launch_dependent(quant_row_block_kernel<T, true>, (unsigned)R, 256, st,
+                       static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale,
+                       reverse);
     else
-      quant_row_block_kernel<T, false><<<(unsigned)R, 256, 0, st>>>(
-          static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale, reverse);
+      launch_dependent(quant_row_block_kernel<T, false>, (unsigned)R, 256, st,
+                       static_cast<const T*>(x), C, q, scale, amax, amax_stride, scalar_scale,
+                       reverse);
     return launch_rc();
   }
   // warps per row; a partial last block only when R % 8 != 0, so reversing
   // whole blocks still covers every row once
   const unsigned blocks = (unsigned)((R + 7) / 8);
   if (vec)
-    quant_rows_kernel<T, true><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
-                                                       amax_stride, reverse);
+    launch_dependent(quant_rows_kernel<T, true>, blocks, 256, st, static_cast<const T*>(x), R, C,
+                     q, scale, amax, amax_stride, reverse);
   else
-    quant_rows_kernel<T, false><<<blocks, 256, 0, st>>>(static_cast<const T*>(x), R, C, q, scale, amax,
-                                                        amax_stride, reverse);
+    launch_dependent(quant_rows_kernel<T, false>, blocks, 256, st, static_cast<const T*>(x), R, C,
+                     q, scale, amax, amax_stride, reverse);
   return launch_rc();
 }
 
