@@ -130,13 +130,13 @@ __device__ __forceinline__ void pdl_release() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
-inline void launch_dependent_smem(void (*kern)(KArgs...), unsigned grid, unsigned block,
+inline void launch_dependent_smem(void (*kern)(KArgs...), dim3 grid, unsigned block,
                                   size_t smem, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -21,8 +21,8 @@
 // their launch overlaps the previous
 // kernel's tail (e.g. the previous layer's GEMM, which reads the int8
 // activations this kernel is about to write).
-// The one-row-per-block quantiser is launched so (8192 x 4096 fp32 per token
-// 20.5 -> 19.2 us, per-channel 14336 x 4096 40.8 -> 39.2 us, B200); the
+// The one-row-per-block quantiser is launched so (8192 x 4096 bf16 per token
+// 20.5 -> 19.2 us, per-channel 14336 x 4096 fp32 40.8 -> 39.2 us, B200); the
 // one-cluster per-tensor quantiser is not: its cluster of 16 CTAs waiting
 // beside the previous GEMM made the 128 x 2048 x 11008 linear layer 0.4 us
 // slower.  Its griddepcontrol.wait then returns at once.
@@ -364,6 +364,7 @@ __global__ void __launch_bounds__(256) colmajor_quant_kernel(const T* __restrict
                                                              int8_t* __restrict__ q,
                                                              float* __restrict__ scale) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
+  pdl_wait();
   __shared__ __align__(16) int8_t tile[64][64 + 16];
   __shared__ float srow[64];
   const int m0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
@@ -473,6 +474,7 @@ __global__ void __launch_bounds__(256) colmajor_quant_vec_kernel(const T* __rest
                                                                  float* __restrict__ scale,
                                                                  int reverse) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // see kPdlNote
+  pdl_wait();
   __shared__ uint32_t tile[64][17];
   __shared__ float srow[64];
   const unsigned nb = gridDim.x * gridDim.y;
@@ -755,11 +757,13 @@ void colmajor_quant_launch(const void* x, int M, int K, const uint32_t* amax, in
                            int8_t* q, float* scale, int reverse, cudaStream_t st) {
   const T* xt = static_cast<const T*>(x);
   const dim3 grid((M + 63) / 64, (K + 63) / 64);
+  // the quantise pass follows the max pass as a programmatic dependent
   if (colmajor_vec_ok<T>(x, M))
-    colmajor_quant_vec_kernel<T><<<grid, 256, 0, st>>>(xt, M, K, amax, amax_stride, q, scale,
-                                                       reverse);
+    launch_dependent_smem(colmajor_quant_vec_kernel<T>, grid, 256, 0, st, xt, M, K, amax,
+                          amax_stride, q, scale, reverse);
   else
-    colmajor_quant_kernel<T><<<grid, 256, 0, st>>>(xt, M, K, amax, amax_stride, q, scale);
+    launch_dependent_smem(colmajor_quant_kernel<T>, grid, 256, 0, st, xt, M, K, amax,
+                          amax_stride, q, scale);
 }
 
 template <typename T>
